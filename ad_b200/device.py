@@ -1,0 +1,363 @@
+"""``CudaB200Device``: the reference's device plug-in, backed by sm_100a kernels.
+
+Drop-in for ``autodiff.device.opencl.OpenCLDevice`` (autodiff/device/opencl/
+device.py:9-146): same duck-typed methods ``init(cmd)``, ``run(cmd)``,
+``_run_proc(proc, func, init)``, ``execute(proc)``, and the same observable
+behaviour -- Feeder ``func()`` called once per iteration and its result
+asserted to be an ``np.ndarray`` of the declared shape (device.py:98-101),
+Receiver callbacks called with freshly allocated numpy arrays in program order
+(device.py:102-110), exceptions from callbacks propagate out of ``execute``.
+
+What is different (B200-native):
+
+* one arena allocation planned by ``memplan`` (256-byte aligned, kernel-
+  granularity lifetimes) instead of one buffer per AllocEntry;
+* every compute command becomes a generated sm_100a kernel (``codegen``,
+  ``gemm``) compiled by NVRTC in parallel during ``init``;
+* ``ForNode`` bodies are captured once into a CUDA graph and replayed
+  (``len(r)`` launches instead of ``len(r) * n_kernels`` Python launches); the
+  Feeder's host-to-device copy is a node of that graph reading a pinned
+  staging buffer, double-buffered so the host prepares iteration i+1 while
+  the GPU runs iteration i;
+* optional data parallelism: ``dist`` inserts gradient all-reduces.
+
+There is no CPU fallback: if the CUDA library or a GPU is missing, the
+constructor raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import time
+from concurrent.futures import ThreadPoolExecutor
+from typing import Callable, Dict, List, Optional
+
+import numpy as np
+
+from . import codegen, ir, memplan
+from . import runtime as rt
+
+ELEMENTWISE = ("ElwFuse", "BinaryNode", "UnaryNode", "ContigiousNode")
+REDUCE = ("ReduceNode", "ReduceElwFuse")
+DOT = ("DotProdNode", "DPElwFuse")
+
+
+class Launch:
+    """A compiled kernel with its bound arguments (the reference's ``funcs[pid]``
+    closure from build_kernel, cl_helper.py:445-455)."""
+    __slots__ = ("spec", "kernel", "args", "argv", "holders")
+
+    def __init__(self, spec: codegen.KernelSpec, kernel: rt.Kernel, ptrs: List[int], extra=None):
+        self.spec = spec
+        self.kernel = kernel
+        holders = [ctypes.c_uint64(p) for p in ptrs]
+        if extra:
+            holders += extra
+        self.holders = holders
+        self.argv = (ctypes.c_void_p * max(1, len(holders)))(
+            *[ctypes.cast(ctypes.byref(h), ctypes.c_void_p) for h in holders])
+
+
+class CudaB200Device:
+    """Device plug-in with the reference's interface (device/__init__.py:1-6)."""
+
+    def __init__(self, device: int = 0, use_graphs: bool = True, gemm: str = "auto",
+                 verbose: bool = False, comm=None):
+        self.ctx = rt.Context(device)
+        self.use_graphs = use_graphs and os.environ.get("AD_GRAPH", "1") != "0"
+        self.gemm = os.environ.get("AD_GEMM", gemm)
+        self.verbose = verbose
+        self.comm = comm
+        self.arena = 0
+        self.arena_bytes = 0
+        self.slots: Dict[int, memplan.Slot] = {}
+        self.launches: Dict[int, List[Launch]] = {}   # id(cmd) -> launches
+        self.kernels: Dict[str, rt.Kernel] = {}
+        self._graphs: Dict[int, list] = {}
+        self._staging: Dict[int, list] = {}
+        self.n_launches = 0
+        self.compile_seconds = 0.0
+        self.proc: Optional[ir.Proc] = None
+
+    # ------------------------------------------------------------ memory
+    def ptr(self, buf_id: int) -> int:
+        return self.arena + self.slots[buf_id].offset
+
+    def _setup_memory(self, proc: ir.Proc) -> None:
+        self.slots, total = memplan.plan(proc)
+        self.scratch_bytes = 0
+        self.arena_bytes = total
+        self.arena = self.ctx.malloc(max(total, 256))
+        for c in ir.iter_cmds(proc):
+            if isinstance(c, ir.AllocEntry) and not c.is_temp and c.content is not None:
+                a = np.ascontiguousarray(np.asarray(c.content, dtype=np.float32).reshape(-1))
+                assert a.size <= c.size
+                self.ctx.h2d(self.ptr(c.id), a.ctypes.data, a.nbytes, 0)
+                self.ctx.sync(0)
+
+    def upload(self, buf_id: int, arr: np.ndarray, offset: int = 0) -> None:
+        a = np.ascontiguousarray(arr, dtype=np.float32)
+        self.ctx.h2d(self.ptr(buf_id) + 4 * offset, a.ctypes.data, a.nbytes, 0)
+        self.ctx.sync(0)
+
+    def download(self, buf_id: int, n: Optional[int] = None, offset: int = 0) -> np.ndarray:
+        n = self.slots[buf_id].size - offset if n is None else n
+        out = np.empty(n, dtype=np.float32)
+        self.ctx.sync(0)
+        self.ctx.d2h(out.ctypes.data, self.ptr(buf_id) + 4 * offset, out.nbytes, 0)
+        self.ctx.sync(0)
+        return out
+
+    # ------------------------------------------------------------ init pass
+    def _specs_for(self, cmd) -> List[codegen.KernelSpec]:
+        kind = type(cmd).__name__
+        sizes = {b: s.size for b, s in self.slots.items()}
+        name = f"k_{kind}"
+        if kind in ELEMENTWISE:
+            return [codegen.gen_elementwise(cmd, name, sizes)]
+        if kind in REDUCE:
+            return [codegen.gen_reduce(cmd, name, sizes)]
+        if kind in DOT:
+            from . import gemm
+            return gemm.plan_dot(self, cmd, name, sizes)
+        raise TypeError(f"Encountered unexpected cmd: {kind}")
+
+    def init(self, cmd) -> None:
+        """Per-command init (opencl/device.py:46-86): kernels are generated here
+        and compiled in one parallel batch by ``_compile_pending``."""
+        kind = type(cmd).__name__
+        if kind in ("Feeder", "Receiver"):
+            ks = [cmd.kres] if kind == "Feeder" else cmd.kargs
+            for k in ks:
+                off = offset_of(k)
+                n = math.prod(k.shape)
+                if off < 0 or off + n > self.slots[k.id].size:
+                    raise ValueError(f"{kind} access out of range for buffer {k.id}")
+            return
+        if kind in ("AllocEntry", "DeallocEntry", "ForNode"):
+            return
+        self._pending.append((cmd, self._specs_for(cmd)))
+
+    def _compile_pending(self) -> None:
+        todo = {}
+        for _, specs in self._pending:
+            for s in specs:
+                if s.src not in self.kernels and s.src not in todo:
+                    todo[s.src] = s
+        t0 = time.time()
+        srcs = list(todo.values())
+        with ThreadPoolExecutor(max_workers=min(16, max(1, len(srcs)))) as ex:
+            cubins = list(ex.map(lambda s: rt.compile_cubin(s.src, s.name + ".cu"), srcs))
+        for s, cub in zip(srcs, cubins):
+            k = self.ctx.load(cub, s.name)
+            if s.smem > 48 * 1024:
+                k.set_smem(s.smem)
+            self.kernels[s.src] = k
+        self.compile_seconds += time.time() - t0
+        for cmd, specs in self._pending:
+            ls = []
+            for s in specs:
+                ptrs = [self.ptr(b) if b >= 0 else self.scratch_ptr(b) for b in s.buffers]
+                extra = s.extra.get("args")
+                ls.append(Launch(s, self.kernels[s.src], ptrs, extra))
+            self.launches[id(cmd)] = ls
+        self._pending = []
+
+    def scratch_ptr(self, b: int) -> int:
+        return self.scratch[b]
+
+    # ------------------------------------------------------------ run pass
+    def _launch(self, L: Launch, stream: int = 0) -> None:
+        s = L.spec
+        self.ctx.launch(L.kernel, s.grid, s.block, s.smem, L.argv, stream)
+        self.n_launches += 1
+
+    def run(self, cmd) -> None:
+        """Per-command run (opencl/device.py:88-112)."""
+        kind = type(cmd).__name__
+        if kind in ("AllocEntry", "DeallocEntry", "ForNode"):
+            return
+        if kind == "Feeder":
+            arr = cmd.func()
+            assert isinstance(arr, np.ndarray) and list(arr.shape) == list(cmd.shape), "Invalid function"
+            a = np.ascontiguousarray(arr, dtype=np.float32)
+            self.ctx.h2d(self.ptr(cmd.kres.id) + 4 * offset_of(cmd.kres), a.ctypes.data, a.nbytes, 0)
+            self.ctx.sync(0)  # the numpy array may be freed once we return
+            return
+        if kind == "Receiver":
+            outs = []
+            self.ctx.sync(0)
+            for k in cmd.kargs:
+                n = math.prod(k.shape)
+                o = np.empty(n, dtype=np.float32)
+                self.ctx.d2h(o.ctypes.data, self.ptr(k.id) + 4 * offset_of(k), 4 * n, 0)
+                outs.append(o)
+            self.ctx.sync(0)
+            outs = [o.reshape(k.shape) for o, k in zip(outs, cmd.kargs)]
+            self.last_received = outs
+            if cmd.func is not None:
+                cmd.func(*outs)
+            return
+        if kind == "AllReduce":
+            cmd.run(self)
+            return
+        for L in self.launches[id(cmd)]:
+            self._launch(L)
+
+    def _run_proc(self, proc: ir.Proc, func: Callable, init: bool = False) -> None:
+        """opencl/device.py:114-124, with ForNode bodies replayed as CUDA graphs."""
+        for cmd in proc.procedure:
+            if isinstance(cmd, ir.ForNode):
+                if init:
+                    self._run_proc(cmd.proc, func, init)
+                elif self.use_graphs and graphable(cmd.proc):
+                    self._replay_graph(cmd)
+                else:
+                    for _ in cmd.r:
+                        self._run_proc(cmd.proc, func, init)
+            else:
+                func(cmd)
+
+    # ------------------------------------------------------------ graphs
+    def _capture(self, body: ir.Proc, staging: Dict[int, np.ndarray]):
+        """Capture one replay of ``body`` (no Receivers) into a CUDA graph.
+        Feeder copies read from ``staging`` (pinned host arrays)."""
+        rt.graph_begin(self.ctx, 0)
+        try:
+            for cmd in body.procedure:
+                kind = type(cmd).__name__
+                if kind == "Feeder":
+                    a = staging[id(cmd)]
+                    self.ctx.h2d(self.ptr(cmd.kres.id) + 4 * offset_of(cmd.kres), a.ctypes.data, a.nbytes, 0)
+                elif kind in ("AllocEntry", "DeallocEntry"):
+                    continue
+                elif kind == "ForNode":
+                    for _ in cmd.r:
+                        self._capture_inline(cmd.proc, staging)
+                else:
+                    self.run(cmd)
+        except Exception:
+            try:
+                rt.graph_end(self.ctx, 0)
+            except Exception:
+                pass
+            raise
+        return rt.graph_end(self.ctx, 0)
+
+    def _capture_inline(self, body, staging):
+        for cmd in body.procedure:
+            kind = type(cmd).__name__
+            if kind == "Feeder":
+                a = staging[id(cmd)]
+                self.ctx.h2d(self.ptr(cmd.kres.id) + 4 * offset_of(cmd.kres), a.ctypes.data, a.nbytes, 0)
+            elif kind == "ForNode":
+                for _ in cmd.r:
+                    self._capture_inline(cmd.proc, staging)
+            elif kind not in ("AllocEntry", "DeallocEntry"):
+                self.run(cmd)
+
+    def _pinned(self, nbytes: int) -> np.ndarray:
+        p = ctypes.c_void_p()
+        rt.check(self.ctx.L.ad_pinned_alloc(nbytes, ctypes.byref(p)), "ad_pinned_alloc")
+        self._pinned_ptrs.append(p.value)
+        return np.ctypeslib.as_array((ctypes.c_float * (nbytes // 4)).from_address(p.value))
+
+    def _replay_graph(self, loop: ir.ForNode) -> None:
+        feeders = [c for c in ir.iter_cmds(loop.proc) if type(c).__name__ == "Feeder"]
+        key = id(loop)
+        if key not in self._graphs:
+            pairs = []
+            for _ in range(2 if feeders else 1):
+                staging = {id(f): self._pinned(4 * math.prod(f.shape)) for f in feeders}
+                g = self._capture(loop.proc, staging)
+                done = self.ctx.event(False)
+                pairs.append((g, staging, done, [False]))
+            self._graphs[key] = pairs
+        pairs = self._graphs[key]
+        n_kern = sum(len(self.launches.get(id(c), [])) for c in ir.iter_cmds(loop.proc))
+        for i in range(len(loop.r)):
+            g, staging, done, used = pairs[i % len(pairs)]
+            if feeders:
+                if used[0]:
+                    done.sync()  # the copy that read this staging slot has finished
+                for f in feeders:
+                    arr = f.func()
+                    assert isinstance(arr, np.ndarray) and list(arr.shape) == list(f.shape), "Invalid function"
+                    staging[id(f)][:] = np.asarray(arr, dtype=np.float32).reshape(-1)
+            g.launch(0)
+            self.n_launches += n_kern
+            if feeders:
+                done.record(0)
+                used[0] = True
+
+    # ------------------------------------------------------------ entry point
+    def prepare(self, proc) -> ir.Proc:
+        """Init pass: plan + allocate memory, upload contents, build all kernels."""
+        proc = ir.conv_proc(proc)
+        self.proc = proc
+        self._pinned_ptrs: List[int] = []
+        self._setup_memory(proc)
+        from . import gemm
+        gemm.setup_scratch(self, proc)
+        self._pending = []
+        self._run_proc(proc, self.init, init=True)
+        self._compile_pending()
+        return proc
+
+    def execute(self, proc) -> None:
+        """opencl/device.py:126-130: init pass, run pass, wait for the queue."""
+        proc = self.prepare(proc)
+        self._run_proc(proc, self.run, init=False)
+        self.ctx.sync()
+
+    def replay(self, cmds: Optional[List] = None) -> None:
+        """Re-launch the compute commands of the prepared proc (no host I/O)."""
+        for c in (cmds if cmds is not None else self.proc.procedure):
+            if type(c).__name__ in ir.COMPUTE_KINDS:
+                self.run(c)
+
+    def close(self) -> None:
+        if getattr(self, "ctx", None) is None:
+            return
+        self._graphs = {}
+        try:
+            self.ctx.sync()
+        except Exception:
+            pass
+        for p in getattr(self, "_pinned_ptrs", []):
+            self.ctx.L.ad_pinned_free(ctypes.c_void_p(p))
+        self._pinned_ptrs = []
+        for k in self.kernels.values():
+            self.ctx.L.ad_kernel_free(k.h)
+        self.kernels = {}
+        if self.arena:
+            self.ctx.free(self.arena)
+            self.arena = 0
+        for p in getattr(self, "scratch_allocs", []):
+            self.ctx.free(p)
+        self.scratch_allocs = []
+        self.ctx.close()
+        self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def graphable(p: ir.Proc) -> bool:
+    return not any(type(c).__name__ == "Receiver" for c in ir.iter_cmds(p))
+
+
+def offset_of(k) -> int:
+    """``KMatrix.calc_offset`` (autodiff/kernalize/__init__.py:74-83)."""
+    a = k.access
+    if isinstance(a, ir.Gid):
+        return 0
+    if isinstance(a, ir.Bin) and a.op == "Add" and isinstance(a.a, ir.Gid) and isinstance(a.b, ir.Const):
+        return a.b.val
+    if isinstance(a, ir.Const) and math.prod(k.shape) == 1:
+        return a.val
+    raise Exception(f"Invalid Feeder setting: {ir.expr_str(a)}. Make sure to call .contigious before Global() ")

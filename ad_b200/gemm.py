@@ -1,0 +1,53 @@
+"""Dot products (``DotProdNode`` / ``DPElwFuse``) on B200.
+
+The reference computes ``C[ty, tx] = sum_k A(_x=ty, _y=k) * B(_x=k, _y=tx)``
+one output per work item (opencl/kernels/dotprod.py:7-43) and runs the fused
+epilogue with ``_x = ty, _y = tx, _global_id = ty * wB + tx``
+(opencl/kernels/dp_elw_fuse.py:11-65).  This module picks the B200 schedule:
+
+* ``simt``: fp32 CUDA-core tiles (``codegen.gen_dot_simt``), for tiny
+  products where a tensor-core tile would be mostly padding.
+* ``tc``: tcgen05 tensor cores with 3xTF32 (see ``tcgen05.py``).
+"""
+from __future__ import annotations
+
+from typing import Dict, List
+
+from . import codegen, ir
+
+
+def use_tensor_cores(dev, M: int, N: int, K: int) -> bool:
+    mode = getattr(dev, "gemm", "auto")
+    if mode == "auto":
+        mode = "simt"
+    if mode == "simt":
+        return False
+    if mode == "tc":
+        return True
+    return M * N * K >= (1 << 21) and min(M, N) >= 16 and K >= 8
+
+
+def plan_dot(dev, cmd, name: str, sizes: Dict[int, int]) -> List[codegen.KernelSpec]:
+    dn, M, N, K = codegen.dot_shape(cmd)
+    if use_tensor_cores(dev, M, N, K):
+        from . import tcgen05
+        return tcgen05.plan(dev, cmd, name, sizes)
+    return [codegen.gen_dot_simt(cmd, name + "_simt", sizes)]
+
+
+def setup_scratch(dev, proc: ir.Proc) -> None:
+    """Scratch for the tensor-core path (split operands), sized for the largest dot."""
+    dev.scratch = {}
+    dev.scratch_allocs = []
+    need = 0
+    for c in ir.iter_cmds(proc):
+        if type(c).__name__ in ("DotProdNode", "DPElwFuse"):
+            dn, M, N, K = codegen.dot_shape(c)
+            if use_tensor_cores(dev, M, N, K):
+                from . import tcgen05
+                need = max(need, tcgen05.scratch_bytes(M, N, K))
+    if need:
+        base = dev.ctx.malloc(need)
+        dev.scratch_allocs.append(base)
+        dev.scratch_base = base
+        dev.scratch_bytes = need

@@ -1,0 +1,330 @@
+"""Benchmark of the B200 device backend on BASELINE.json's configurations.
+
+Default (N=1): config 2, the fused Reduce+elementwise microbench --
+LayerNorm then softmax over the last dim of fp32 [8192, 4096], forward plus
+backward w.r.t. x -- run as the proc the reference front-end produces for it
+(tests/golden/procs/lnsm_8192_4096.json.gz).  One step = one pass of every
+compute command of that proc over inputs already resident in HBM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload lnsm|dotsig|mlp]
+    python bench.py --impl reference ...   # the reference's kernels on the host CPU
+
+``value`` = fused-kernel HBM throughput: sum over the step's kernels of their
+algorithmic bytes (unique extents read + written) / step time.  ``e2e`` =
+the same bytes through the public device API with host-resident inputs:
+pinned host->device copy of x and dy, the step, device->host copy of y and dx.
+Multi-GPU (torchrun): every rank runs its own replica ("weak" scaling, no
+data-path collective; the LayerNorm/softmax rows are independent), barrier +
+CUDA-event timing, max over ranks.
+"""
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    "lnsm": {"case": "lnsm_8192_4096", "metric": "fused-kernel HBM GB/s (LayerNorm+softmax fwd+bwd, fp32 [8192,4096])",
+             "unit": "GB/s", "min_bytes": 4 * 8192 * 4096 * 4},
+    "dotsig": {"case": "dotsig_4096", "metric": "fused DotProd+sigmoid fwd+bwd TFLOP/s (fp32 4096^3)",
+               "unit": "TFLOP/s", "flops": 3 * 2 * 4096 ** 3},
+}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=2)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if len(r) > 3 + i and r[3 + i].lower().startswith("active")})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(self.rows)}
+
+
+def dist_env():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def host_group(world):
+    if world == 1:
+        return None
+    import torch.distributed as td
+    td.init_process_group("gloo")
+    return td
+
+
+def allmax(td, v: float) -> float:
+    if td is None:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64)
+    td.all_reduce(t, op=td.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(td):
+    if td is not None:
+        td.barrier()
+
+
+def cpu_reference(args, wl, rank, world):
+    """The reference's kernels (C restatement of its OpenCL kernel bodies, oracle/cexec.py)
+    on the host cores, bounded sample: ``steps`` full steps of the same proc."""
+    if rank != 0:
+        return
+    from ad_b200.fixtures import load_case
+    from oracle.cexec import OracleDevice
+    p, m = load_case(wl["case"])
+    threads = os.cpu_count() or 1
+    d = OracleDevice(threads=threads)
+    d.prepare(p)
+    cmds = [c for c in p.procedure if type(c).__name__ not in ("AllocEntry", "DeallocEntry", "Receiver")]
+    for _ in range(max(1, min(args.warmup, 1))):
+        for c in cmds:
+            d.run_cmd(c)
+    steps = max(1, min(args.steps, args.cpu_steps))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for c in cmds:
+            d.run_cmd(c)
+    dt = (time.perf_counter() - t0) / steps
+    value = step_value(wl, alg_bytes_of(p), dt)
+    line = {"impl": "reference", "metric": wl["metric"], "value": value, "unit": wl["unit"],
+            "n_gpus": world, "steps": steps, "warmup": 1, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded normal inputs)",
+            "config": {"workload": wl["case"]},
+            "cpu_baseline": {"value": value, "unit": wl["unit"], "cores": threads, "kind": "port",
+                             "sample": f"{steps} full step(s) of {wl['case']} on {threads} host threads"},
+            "e2e": {"value": value, "unit": wl["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def alg_bytes_of(p):
+    from ad_b200 import codegen, ir, memplan
+    slots, _ = memplan.plan(p)
+    sizes = {b: s.size for b, s in slots.items()}
+    total = 0
+    for c in ir.iter_cmds(p):
+        k = type(c).__name__
+        if k in ("ElwFuse", "BinaryNode", "UnaryNode", "ContigiousNode"):
+            total += codegen.gen_elementwise(c, "k", sizes).bytes_moved
+        elif k in ("ReduceNode", "ReduceElwFuse"):
+            total += codegen.gen_reduce(c, "k", sizes).bytes_moved
+        elif k in ("DotProdNode", "DPElwFuse"):
+            _, M, N, K = codegen.dot_shape(c)
+            total += 4 * (M * K + K * N + M * N)
+    return total
+
+
+def step_value(wl, alg_bytes, seconds):
+    if wl["unit"] == "GB/s":
+        return alg_bytes / seconds / 1e9
+    return wl["flops"] / seconds / 1e12
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="lnsm", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    wl = WORKLOADS[args.workload]
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        cpu_reference(args, wl, rank, world)
+        return
+
+    td = host_group(world)
+    from ad_b200 import ir
+    from ad_b200.device import CudaB200Device
+    from ad_b200.fixtures import load_case
+    from ad_b200 import runtime as rt
+
+    p, meta = load_case(wl["case"])
+    dev = CudaB200Device(local)
+    proc = dev.prepare(p)
+    cmds = [c for c in proc.procedure if type(c).__name__ in ir.COMPUTE_KINDS]
+    launches = [L for c in cmds for L in dev.launches[id(c)]]
+    alg_bytes = sum(L.spec.bytes_moved for L in launches)
+    ctx = dev.ctx
+
+    # per-kernel events inside the timed region (stream 0 is the launching stream)
+    ev = [[ctx.event(True) for _ in range(len(launches) + 1)] for _ in range(args.steps)]
+    for _ in range(args.warmup):
+        dev.replay(cmds)
+    ctx.sync()
+    barrier(td)
+    start, end = ctx.event(True), ctx.event(True)
+    with ClockSampler(local) as clk:
+        ctx.sync()
+        start.record(0)
+        for s in range(args.steps):
+            ev[s][0].record(0)
+            for i, L in enumerate(launches):
+                dev._launch(L)
+                ev[s][i + 1].record(0)
+        end.record(0)
+        end.sync()
+    total_ms = start.elapsed_ms(end)
+    per_kernel = np.zeros(len(launches))
+    for s in range(args.steps):
+        for i in range(len(launches)):
+            per_kernel[i] += ev[s][i].elapsed_ms(ev[s][i + 1])
+    per_kernel /= args.steps
+    ms = allmax(td, total_ms / args.steps)
+    value = step_value(wl, alg_bytes, ms / 1e3) * world
+
+    # roofline of the dominant kernel
+    hbm, bf16, peak_kind = peaks()
+    top = int(np.argmax(per_kernel))
+    Lt = launches[top]
+    achieved = Lt.spec.bytes_moved / (per_kernel[top] / 1e3) / 1e9
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", f"traffic_{wl['case']}.json")
+    if os.path.exists(tfile):
+        with open(tfile) as f:
+            traffic = json.load(f).get(str(top))
+
+    # e2e through the public API with host-resident inputs (pinned)
+    in_ids = [meta[k] for k in ("x_id", "dy_id") if k in meta]
+    recv = [c for c in proc.procedure if type(c).__name__ == "Receiver"]
+    out_refs = [(k.id, int(np.prod(k.shape))) for r in recv for k in r.kargs]
+    host_in = {}
+    for b in in_ids:
+        a = dev._pinned(4 * dev.slots[b].size)
+        a[:] = 0.5
+        host_in[b] = a
+    host_out = [dev._pinned(4 * n) for _, n in out_refs]
+    e2e_steps = max(3, args.steps // 2)
+
+    def e2e_step():
+        for b, a in host_in.items():
+            ctx.h2d(dev.ptr(b), a.ctypes.data, a.nbytes, 0)
+        dev.replay(cmds)
+        for (b, n), o in zip(out_refs, host_out):
+            ctx.d2h(o.ctypes.data, dev.ptr(b), 4 * n, 0)
+
+    e2e_step()
+    ctx.sync()
+    barrier(td)
+    e0, e1 = ctx.event(True), ctx.event(True)
+    e0.record(0)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(0)
+    e1.sync()
+    e2e_ms = allmax(td, e0.elapsed_ms(e1) / e2e_steps)
+    h2d = sum(a.nbytes for a in host_in.values())
+    d2h = sum(o.nbytes for o in host_out)
+
+    if rank == 0:
+        line = {
+            "metric": wl["metric"], "value": value, "unit": wl["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: x ~ N(0,1) seed 0, dy ~ N(0,1) seed 1 (numpy default_rng)",
+            "config": {"workload": wl["case"], "alg_bytes_per_step": alg_bytes,
+                       "min_bytes_per_step": wl.get("min_bytes"),
+                       "min_traffic_GBps": (wl.get("min_bytes") or 0) / (ms / 1e3) / 1e9,
+                       "kernels_per_step": len(launches), "l2": "inputs larger than L2 (128 MiB each)",
+                       "parallelism": f"replicas x{world}"},
+            "gpu_launches": len(launches) * args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": f"{top}:{Lt.spec.kind}", "kernel_ms": per_kernel[top],
+                         "alg_bytes": Lt.spec.bytes_moved},
+            "per_kernel_ms": [round(float(x), 4) for x in per_kernel],
+            "per_kernel_GBps": [round(L.spec.bytes_moved / (t / 1e3) / 1e9, 1) for L, t in zip(launches, per_kernel)],
+            "clocks": clk.summary(),
+            "e2e": {"value": step_value(wl, alg_bytes, e2e_ms / 1e3) * world, "unit": wl["unit"],
+                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "compile_s": round(dev.compile_seconds, 2),
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(wl, p)
+        print(json.dumps(line), flush=True)
+    dev.close()
+    barrier(td)
+
+
+def cpu_baseline(wl, p):
+    from oracle.cexec import OracleDevice
+    threads = os.cpu_count() or 1
+    d = OracleDevice(threads=threads)
+    d.prepare(p)
+    cmds = [c for c in p.procedure if type(c).__name__ not in ("AllocEntry", "DeallocEntry", "Receiver")]
+    for c in cmds:
+        d.run_cmd(c)
+    t0 = time.perf_counter()
+    n = 0
+    while n < 2 and time.perf_counter() - t0 < 20:
+        for c in cmds:
+            d.run_cmd(c)
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return {"value": step_value(wl, alg_bytes_of(p), dt), "unit": wl["unit"], "cores": threads,
+            "kind": "port", "sample": f"{n} full step(s) of {wl['case']} (C restatement of the reference kernels, OpenMP)"}
+
+
+if __name__ == "__main__":
+    main()
