@@ -181,23 +181,28 @@ def index_type(c, rng) -> str:
 
 
 def written_reads_bytes(c, rng, sizes: Dict[int, int]) -> int:
-    """Algorithmic bytes: for each buffer, the extent of its touched address range
-    (capped at the buffer size), counted once for reads and once for writes."""
+    """Algorithmic HBM bytes of one launch: for each buffer, the extent of the
+    address range it touches (capped at the buffer size), once if read and once
+    if written.  A read of a buffer that an earlier statement of the same
+    kernel already wrote (same thread, read-after-write) costs no DRAM traffic
+    and is not counted."""
     reads: Dict[int, Tuple[int, int]] = {}
     writes: Dict[int, Tuple[int, int]] = {}
 
-    def note(d, k):
+    def note(d, k, skip=()):
         if isinstance(k, ir.KMatrix) and not k.is_temp:
+            if k.id in skip:
+                return
             lo, hi = exprs.bounds(k.access, rng)
             o = d.get(k.id)
             d[k.id] = (lo, hi) if o is None else (min(o[0], lo), max(o[1], hi))
         elif isinstance(k, ir.KConcat):
-            note(d, k.karg_one)
-            note(d, k.karg_two)
+            note(d, k.karg_one, skip)
+            note(d, k.karg_two, skip)
 
     for n in chain_nodes(c):
         for k in n.kargs:
-            note(reads, k)
+            note(reads, k, skip=writes)
         note(writes, n.kres)
     total = 0
     for d in (reads, writes):
@@ -452,12 +457,20 @@ def gen_reduce(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
         block = gs * rows_per_block
         warps_per_group = gs // 32
         env = {"X": "xr", "Y": "yy", "G": "xr"}
+        upt_all = (units + gs - 1) // gs
+        upt = min(upt_all, 8)          # loads per thread in flight before combining
+        chunks = (upt_all + upt - 1) // upt
         if row_vec:
-            load = (f"{{ const float4 q = *reinterpret_cast<const float4*>(&{em.p(src_k.id)}"
-                    f"[{em.expr(src_k.access, env)}]);\n"
-                    f"                acc = {comb(comb('acc', 'q.x'), comb('q.y', comb('q.z', 'q.w')))}; }}")
+            ldv = (f"*reinterpret_cast<const float4*>(&{em.p(src_k.id)}[{em.expr(src_k.access, env)}])")
+            load_stmt = f"if (yy < ({it}){R}) q[u] = {ldv};"
+            fold = f"acc = {comb(comb('acc', 'q[u].x'), comb('q[u].y', comb('q[u].z', 'q[u].w')))};"
+            qdecl = f"float4 q[{upt}];"
+            qinit = f"q[u] = make_float4({ident}, {ident}, {ident}, {ident});"
         else:
-            load = f"acc = {comb('acc', em.scalar_karg(src_k, env, {}))};"
+            load_stmt = f"if (yy < ({it}){R}) q[u] = {em.scalar_karg(src_k, env, {})};"
+            fold = f"acc = {comb('acc', 'q[u]')};"
+            qdecl = f"float q[{upt}];"
+            qinit = f"q[u] = {ident};"
         shfl = comb("acc", "__shfl_xor_sync(0xffffffffu, acc, o)")
         cross = ""
         if warps_per_group > 1:
@@ -479,10 +492,19 @@ def gen_reduce(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
     const {it} xr = ({it})blockIdx.x * {rows_per_block} + threadIdx.x / {gs};
     const bool live = xr < ({it}){V};
     float acc = {ident};
-    if (live) {{
-        for ({it} yy = ({it})tig * {per}; yy < ({it}){R}; yy += {gs * per}) {{
-                {load}
+    {qdecl}
+    for (int ch = 0; ch < {chunks}; ++ch) {{
+        #pragma unroll
+        for (int u = 0; u < {upt}; ++u) {{ {qinit} }}
+        if (live) {{
+            #pragma unroll
+            for (int u = 0; u < {upt}; ++u) {{
+                const {it} yy = (({it})tig + ({it})(ch * {upt} + u) * {gs}) * {per};
+                {load_stmt}
+            }}
         }}
+        #pragma unroll
+        for (int u = 0; u < {upt}; ++u) {{ {fold} }}
     }}
     #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc = {shfl};{cross}

@@ -51,12 +51,12 @@ class Launch:
     def __init__(self, spec: codegen.KernelSpec, kernel: rt.Kernel, ptrs: List[int], extra=None):
         self.spec = spec
         self.kernel = kernel
-        holders = [ctypes.c_uint64(p) for p in ptrs]
-        if extra:
-            holders += extra
+        extra = extra or {}
+        holders = list(extra.get("prefix", [])) + [ctypes.c_uint64(p) for p in ptrs] + \
+            list(extra.get("suffix", []))
         self.holders = holders
         self.argv = (ctypes.c_void_p * max(1, len(holders)))(
-            *[ctypes.cast(ctypes.byref(h), ctypes.c_void_p) for h in holders])
+            *[ctypes.addressof(h) for h in holders])
 
 
 class CudaB200Device:
@@ -159,8 +159,7 @@ class CudaB200Device:
             ls = []
             for s in specs:
                 ptrs = [self.ptr(b) if b >= 0 else self.scratch_ptr(b) for b in s.buffers]
-                extra = s.extra.get("args")
-                ls.append(Launch(s, self.kernels[s.src], ptrs, extra))
+                ls.append(Launch(s, self.kernels[s.src], ptrs, s.extra))
             self.launches[id(cmd)] = ls
         self._pending = []
 
@@ -298,6 +297,9 @@ class CudaB200Device:
         self.proc = proc
         self._pinned_ptrs: List[int] = []
         self._setup_memory(proc)
+        self.err_ptr = self.ctx.malloc(256)
+        self.ctx.memset(self.err_ptr, 0, 256, 0)
+        self.scratch_allocs = [self.err_ptr]
         from . import gemm
         gemm.setup_scratch(self, proc)
         self._pending = []
@@ -310,6 +312,18 @@ class CudaB200Device:
         proc = self.prepare(proc)
         self._run_proc(proc, self.run, init=False)
         self.ctx.sync()
+        self.check_errors()
+
+    def check_errors(self) -> None:
+        """Raise if a kernel recorded a device-side error (a bounded wait that
+        expired: 1 = TMA ring stalled, 2 = operand tile never arrived,
+        3 = accumulator never completed)."""
+        flag = np.zeros(1, dtype=np.int32)
+        self.ctx.sync()
+        self.ctx.d2h(flag.ctypes.data, self.err_ptr, 4, 0)
+        self.ctx.sync(0)
+        if flag[0] != 0:
+            raise rt.ADError(f"device kernel reported error code {int(flag[0])} (bounded wait expired)")
 
     def replay(self, cmds: Optional[List] = None) -> None:
         """Re-launch the compute commands of the prepared proc (no host I/O)."""

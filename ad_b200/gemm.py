@@ -18,8 +18,6 @@ from . import codegen, ir
 
 def use_tensor_cores(dev, M: int, N: int, K: int) -> bool:
     mode = getattr(dev, "gemm", "auto")
-    if mode == "auto":
-        mode = "simt"
     if mode == "simt":
         return False
     if mode == "tc":
@@ -38,7 +36,6 @@ def plan_dot(dev, cmd, name: str, sizes: Dict[int, int]) -> List[codegen.KernelS
 def setup_scratch(dev, proc: ir.Proc) -> None:
     """Scratch for the tensor-core path (split operands), sized for the largest dot."""
     dev.scratch = {}
-    dev.scratch_allocs = []
     need = 0
     for c in ir.iter_cmds(proc):
         if type(c).__name__ in ("DotProdNode", "DPElwFuse"):

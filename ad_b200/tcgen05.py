@@ -1,0 +1,358 @@
+"""Dot products on the 5th-generation tensor cores (tcgen05 + TMEM), 3xTF32.
+
+Reference semantics: ``C[ty,tx] = sum_k A(_x=ty,_y=k) * B(_x=k,_y=tx)`` in fp32
+(autodiff/device/opencl/kernels/dotprod.py:7-43) with the fused epilogue of
+dp_elw_fuse.py:11-65.  B200 schedule, three launches per dot:
+
+1. ``split A`` / ``split B``: gather each operand through its access
+   expression (any folded Permute/View/Broadcast/Concat, or a constant),
+   transposing through shared memory when the operand is MN-contiguous, and
+   write it K-major, zero-padded to the tile grid, as two fp32 arrays:
+   ``hi = tf32_rn(x)`` and ``lo = tf32_rn(x - hi)``.
+2. ``gemm``: one CTA per 128 x BN output tile.  Warp 0 lane 0 issues TMA
+   loads (SWIZZLE_128B, 32 fp32 of K per row) of A_hi, A_lo, B_hi, B_lo into a
+   ``STAGES``-deep ring; warp 1 lane 0 issues, per 8-deep K slice,
+   ``A_hi*B_hi + A_hi*B_lo + A_lo*B_hi`` as three ``tcgen05.mma.kind::tf32``
+   into one fp32 TMEM accumulator (the published 3xTF32 split; the dropped
+   ``lo*lo`` term is below fp32 rounding), and ``tcgen05.commit`` releases each
+   stage.  All four warps then read TMEM (``tcgen05.ld.32x32b.x32``),
+   transpose 32x32 blocks through shared memory so that stores are coalesced,
+   and run the fused elementwise epilogue per element.
+
+Every mbarrier wait is bounded; on timeout the kernel records an error code
+in a device flag, stops issuing work, frees its TMEM and returns.
+No TMA multicast is used anywhere.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List
+
+from . import codegen, exprs, ir
+from .codegen import Emitter, KernelSpec, cmd_buffers, dot_epilogue, dot_shape, index_type
+
+BM = 128
+BK = 32                 # fp32 elements of K per stage row = 128 bytes (SWIZZLE_128B)
+BN_DEFAULT = 256
+STAGES_FOR_BN = {256: 2, 128: 3, 64: 4}
+
+
+def pad(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+def tile_n(N: int) -> int:
+    return 256 if N > 128 else (128 if N > 64 else 64)
+
+
+def scratch_bytes(M: int, N: int, K: int) -> int:
+    bn = tile_n(N)
+    Mp, Np, Kp = pad(M, BM), pad(N, bn), pad(K, BK)
+    return 2 * 4 * (Mp * Kp + Np * Kp) + 4096
+
+
+# ---------------------------------------------------------------- split kernel
+
+def gen_split(karg: ir.KernelArg, name: str, rows: int, kdim: int, rows_p: int, k_p: int,
+              row_var: str, k_var: str) -> KernelSpec:
+    """Gather operand(row, k) via its access expression into K-major hi/lo arrays.
+    ``row_var``/``k_var`` say which of the reference's X/Y carries row and k."""
+    bufs = sorted(set(karg.ids(True)))
+    rng = {"X": (0, max(rows, kdim)), "Y": (0, max(rows, kdim)), "G": (0, 0)}
+    it = "int"
+    for e in _karg_exprs(karg):
+        if exprs.subexpr_max(e, rng) >= (1 << 31) - 64:
+            it = "long long"
+    if rows_p * k_p >= (1 << 31) - 64:
+        it = "long long"
+    em = Emitter(bufs, it)
+    orient = "k"
+    if isinstance(karg, ir.KMatrix) and not karg.is_temp:
+        if exprs.lanes(karg.access, k_var, 4).s == 1:
+            orient = "k"
+        elif exprs.lanes(karg.access, row_var, 4).s == 1:
+            orient = "r"
+    env = {row_var: "gr", k_var: "gk", "G": f"(({it})0)"}
+    val = em.scalar_karg(karg, env, {})
+    params = ", ".join([f"const float* __restrict__ p{i}" for i in range(len(bufs))] +
+                       ["float* __restrict__ hi", "float* __restrict__ lo"])
+    if orient == "k":
+        load = f"""for (int i = threadIdx.y; i < 32; i += 8) {{
+        const {it} gr = r0 + i, gk = k0 + threadIdx.x;
+        t[i][threadIdx.x] = (gr < ({it}){rows} && gk < ({it}){kdim}) ? ({val}) : 0.0f;
+    }}"""
+    else:
+        load = f"""for (int i = threadIdx.y; i < 32; i += 8) {{
+        const {it} gr = r0 + threadIdx.x, gk = k0 + i;
+        t[threadIdx.x][i] = (gr < ({it}){rows} && gk < ({it}){kdim}) ? ({val}) : 0.0f;
+    }}"""
+    src = f"""extern "C" __global__ void __launch_bounds__(256) {name}({params}) {{
+    __shared__ float t[32][33];
+    const {it} r0 = ({it})blockIdx.y * 32, k0 = ({it})blockIdx.x * 32;
+    {load}
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += 8) {{
+        const float x = t[i][threadIdx.x];
+        unsigned h, l;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+        const float r = x - __uint_as_float(h);
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(r));
+        const {it} o = (r0 + i) * ({it}){k_p} + k0 + threadIdx.x;
+        hi[o] = __uint_as_float(h);
+        lo[o] = __uint_as_float(l);
+    }}
+}}
+"""
+    return KernelSpec(name, src, bufs, (k_p // 32, rows_p // 32, 1), (32, 8, 1), 0, "split",
+                      4 * rows * kdim + 8 * rows_p * k_p)
+
+
+def _karg_exprs(k):
+    if isinstance(k, ir.KMatrix) and not k.is_temp:
+        return [k.access]
+    if isinstance(k, ir.KConcat):
+        return [k.condition] + _karg_exprs(k.karg_one) + _karg_exprs(k.karg_two)
+    return []
+
+
+# ---------------------------------------------------------------- gemm kernel
+
+GEMM_TEMPLATE = r"""
+struct __align__(64) TmapT { unsigned long long v[16]; };
+
+#define AD_WAIT_NS 2000000000ull   // 2 s: far above any legitimate wait of one tile
+
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+    return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* b, unsigned cnt) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(b)), "r"(cnt));
+}
+__device__ __forceinline__ bool mbar_try(unsigned long long* b, unsigned phase) {
+    unsigned ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                 " selp.u32 %0, 1, 0, p;\n}" : "=r"(ok) : "r"(smem_u32(b)), "r"(phase) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// bounded wait on an mbarrier phase: false after AD_WAIT_NS without completion
+__device__ __noinline__ bool mbar_wait(unsigned long long* b, unsigned phase) {
+    if (mbar_try(b, phase)) return true;
+    const unsigned long long t0 = gtime();
+    while (true) {
+        for (int i = 0; i < 256; ++i)
+            if (mbar_try(b, phase)) return true;
+        if (gtime() - t0 > AD_WAIT_NS) return false;
+    }
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* b, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const TmapT* map, unsigned long long* bar, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+                 :: "r"(smem_u32(dst)), "l"((unsigned long long)map), "r"(smem_u32(bar)), "r"(c0), "r"(c1) : "memory");
+}
+__device__ __forceinline__ unsigned long long sdesc(const void* p) {
+    // K-major SWIZZLE_128B: start>>4, LBO=16B (unused), SBO=1024B, version 1, layout 2 (128B swizzle)
+    const unsigned long long a = (smem_u32(p) >> 4) & 0x3FFFull;
+    return a | (1ull << 16) | ((1024ull >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+__device__ __forceinline__ void mma_tf32(unsigned tmem, unsigned long long ad, unsigned long long bd, unsigned idesc, unsigned acc) {
+    asm volatile("{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+                 " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}"
+                 :: "r"(tmem), "l"(ad), "l"(bd), "r"(idesc), "r"(acc) : "memory");
+}
+__device__ __forceinline__ void mma_commit(unsigned long long* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+
+extern "C" __global__ void __launch_bounds__(128, 1) NAME(
+    const __grid_constant__ TmapT tAh, const __grid_constant__ TmapT tAl,
+    const __grid_constant__ TmapT tBh, const __grid_constant__ TmapT tBl,
+    PARAMS int* __restrict__ err)
+{
+    constexpr int BN = TILE_N, STAGES = NSTAGES, KB = KBLOCKS;
+    constexpr unsigned A_BYTES = 128 * 128, B_BYTES = BN * 128;
+    constexpr unsigned STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = (unsigned char*)(((unsigned long long)smem_raw + 1023) & ~1023ull);
+    unsigned long long* full = (unsigned long long*)(smem + STAGES * STAGE_BYTES);
+    unsigned long long* empty = full + STAGES;
+    unsigned long long* accb = empty + STAGES;
+    unsigned* tmem_slot = (unsigned*)(accb + 1);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+    volatile int* consumed = abort_flag + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * 128, n0 = blockIdx.x * BN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(accb, 1);
+        *abort_flag = 0;
+        *consumed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const unsigned tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // TMA producer
+        int issued = 0;
+        for (int kb = 0; kb < KB; ++kb) {
+            const int s = kb % STAGES;
+            if (kb >= STAGES) {
+                if (!mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { *abort_flag = 1; atomicExch(err, 1); break; }
+            }
+            if (*abort_flag) break;
+            unsigned char* st = smem + s * STAGE_BYTES;
+            mbar_expect_tx(&full[s], STAGE_BYTES);
+            tma_load_2d(st, &tAh, &full[s], kb * 32, m0);
+            tma_load_2d(st + A_BYTES, &tAl, &full[s], kb * 32, m0);
+            tma_load_2d(st + 2 * A_BYTES, &tBh, &full[s], kb * 32, n0);
+            tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tBl, &full[s], kb * 32, n0);
+            issued = kb + 1;
+        }
+        if (*abort_flag) {
+            // drain: wait (bounded) for the copies this CTA issued but nobody consumed
+            for (int kb = *consumed; kb < issued; ++kb) mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer: D(128 x BN) += A(128 x 8) * B(BN x 8)^T per instruction, both K-major
+        constexpr unsigned IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((unsigned)(BN >> 3) << 17) | ((128u >> 4) << 24);
+        for (int kb = 0; kb < KB; ++kb) {
+            const int s = kb % STAGES;
+            if (!mbar_wait(&full[s], (kb / STAGES) & 1)) { *abort_flag = 1; atomicExch(err, 2); break; }
+            if (*abort_flag) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            unsigned char* st = smem + s * STAGE_BYTES;
+            const unsigned long long ah = sdesc(st), al = sdesc(st + A_BYTES);
+            const unsigned long long bh = sdesc(st + 2 * A_BYTES), bl = sdesc(st + 2 * A_BYTES + B_BYTES);
+            #pragma unroll
+            for (int k8 = 0; k8 < 4; ++k8) {
+                const unsigned long long adv = (unsigned long long)(k8 * 32) >> 4;  // 8 fp32 = 32 bytes
+                const unsigned first = (kb > 0 || k8 > 0) ? 1u : 0u;
+                mma_tf32(tmem, ah + adv, bh + adv, IDESC, first);
+                mma_tf32(tmem, ah + adv, bl + adv, IDESC, 1u);
+                mma_tf32(tmem, al + adv, bh + adv, IDESC, 1u);
+            }
+            mma_commit(&empty[s]);
+            *consumed = kb + 1;
+        }
+        mma_commit(accb);
+    }
+    __syncwarp();
+
+    // ---- epilogue: all 4 warps; warp w owns TMEM lanes (rows) 32w .. 32w+31
+    bool ok = mbar_wait(accb, 0);
+    if (!ok) { atomicExch(err, 3); }
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (ok && !*abort_flag) {
+        float* tr = (float*)smem + warp * (32 * 33);   // stage memory is free now
+        #pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            unsigned r[32];
+            const unsigned taddr = tmem + ((unsigned)(warp * 32) << 16) + (unsigned)(c * 32);
+            asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                  "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+                  "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                  "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                : "r"(taddr));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            #pragma unroll
+            for (int j = 0; j < 32; ++j) tr[lane * 33 + j] = __uint_as_float(r[j]);
+            __syncwarp();
+            #pragma unroll 4
+            for (int i = 0; i < 32; ++i) {
+                const IDX om = (IDX)m0 + warp * 32 + i;
+                const IDX on = (IDX)n0 + c * 32 + lane;
+                if (om < (IDX)M_DIM && on < (IDX)N_DIM) {
+                    const float accv = tr[i * 33 + lane];
+                    EPILOGUE
+                }
+            }
+            __syncwarp();
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+"""
+
+
+def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int) -> KernelSpec:
+    bufs = cmd_buffers(c)
+    rng = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
+    it = index_type(_epi_only(c), rng)
+    em = Emitter(bufs, it)
+    epi = dot_epilogue(c, em, it, "accv", {"X": "om", "Y": "on", "G": f"(om * ({it}){N} + on)"})
+    epi = "\n                    ".join(epi.split("\n"))
+    params = "".join(f"float* __restrict__ p{i}, " for i in range(len(bufs)))
+    kb = pad(K, BK) // BK
+    src = (GEMM_TEMPLATE.replace("NAME", name).replace("PARAMS", params).replace("TILE_N", str(bn))
+           .replace("NSTAGES", str(stages)).replace("KBLOCKS", str(kb)).replace("TMEM_COLS", str(max(32, bn)))
+           .replace("IDX", it).replace("M_DIM", str(M)).replace("N_DIM", str(N)).replace("EPILOGUE", epi))
+    stage_bytes = 2 * 128 * 128 + 2 * bn * 128
+    smem = stages * stage_bytes + 1024 + 256
+    grid = (pad(N, bn) // bn, pad(M, BM) // BM, 1)
+    rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
+    epi_bytes = codegen.written_reads_bytes(_epi_only(c), rngw, {})
+    return KernelSpec(name, src, bufs, grid, (128, 1, 1), smem, "gemm_tcgen05",
+                      4 * (M * K + K * N) + epi_bytes, 2 * M * N * K)
+
+
+class _EpiView:
+    """The epilogue chain of a dot command without the dot node itself."""
+
+    def __init__(self, c):
+        nodes = c.nodes if isinstance(c, ir.FuseGroup) else [c]
+        self.nodes = [n for n in nodes if type(n).__name__ != "DotProdNode"]
+        dn = c if type(c).__name__ == "DotProdNode" else c.init_node
+        self.nodes.append(ir.ContigiousNode(-1, [ir.KConstant(0.0)], dn.kres, dn.shape))
+
+
+def _epi_only(c):
+    v = _EpiView(c)
+    return ir.ElwFuse(v.nodes, 0)
+
+
+def plan(dev, cmd, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
+    from . import runtime as rt
+    dn, M, N, K = dot_shape(cmd)
+    A, B = dn.kargs
+    bn = tile_n(N)
+    stages = STAGES_FOR_BN[bn]
+    Mp, Np, Kp = pad(M, BM), pad(N, bn), pad(K, BK)
+    base = dev.scratch_base
+    a_hi, a_lo = base, base + 4 * Mp * Kp
+    b_hi, b_lo = a_lo + 4 * Mp * Kp, a_lo + 4 * Mp * Kp + 4 * Np * Kp
+    sa = gen_split(A, name + "_splitA", M, K, Mp, Kp, "X", "Y")
+    sb = gen_split(B, name + "_splitB", N, K, Np, Kp, "Y", "X")
+    sa.extra["suffix"] = [ctypes.c_uint64(a_hi), ctypes.c_uint64(a_lo)]
+    sb.extra["suffix"] = [ctypes.c_uint64(b_hi), ctypes.c_uint64(b_lo)]
+    g = gen_gemm(cmd, name + "_tc", M, N, K, bn, stages)
+    maps = [rt.tmap_2d(a_hi, Mp, Kp, 4 * Kp, 128, 32), rt.tmap_2d(a_lo, Mp, Kp, 4 * Kp, 128, 32),
+            rt.tmap_2d(b_hi, Np, Kp, 4 * Kp, bn, 32), rt.tmap_2d(b_lo, Np, Kp, 4 * Kp, bn, 32)]
+    g.extra["prefix"] = [ctypes.create_string_buffer(m, 128) for m in maps]
+    g.extra["suffix"] = [ctypes.c_uint64(dev.err_ptr)]
+    g.flops = 2 * M * N * K
+    return [sa, sb, g]

@@ -1,0 +1,49 @@
+"""tcgen05 3xTF32 dot products vs float64 numpy (B200 only).
+
+Tolerance: |C - C64| <= 1e-4 * (|A| @ |B|) + 1e-5 elementwise, i.e. rel 1e-4
+of the magnitude of the products being summed (fp32-level accuracy)."""
+import numpy as np
+import pytest
+
+from tests.procgen import dot_proc
+
+pytestmark = pytest.mark.gpu
+
+
+def run(proc, gemm):
+    from ad_b200.device import CudaB200Device
+    d = CudaB200Device(gemm=gemm)
+    try:
+        d.execute(proc)
+        return d.last_received[0], [L.spec.kind for ls in d.launches.values() for L in ls]
+    finally:
+        d.close()
+
+
+@pytest.mark.parametrize("M,N,K,tb", [(128, 256, 64, False), (256, 256, 256, True),
+                                      (200, 300, 100, False), (130, 70, 33, True),
+                                      (512, 1024, 768, True), (1, 256, 128, False)])
+@pytest.mark.parametrize("gemm", ["tc", "simt"])
+def test_dot(M, N, K, tb, gemm):
+    rng = np.random.default_rng(M * 7 + N + K)
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (N, K) if tb else (K, N)).astype(np.float32)
+    Bm = B.T if tb else B
+    got, kinds = run(dot_proc(A, B, transpose_b=tb), gemm)
+    if gemm == "tc":
+        assert "gemm_tcgen05" in kinds
+    want = A.astype(np.float64) @ Bm.astype(np.float64)
+    mag = np.abs(A).astype(np.float64) @ np.abs(Bm).astype(np.float64)
+    assert np.all(np.abs(got - want) <= 1e-4 * mag + 1e-5)
+
+
+def test_dot_epilogue_bias_scale():
+    rng = np.random.default_rng(1)
+    M, N, K = 384, 512, 256
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    got, _ = run(dot_proc(A, B, bias=b, epi_scale=-0.5), "tc")
+    want = (A.astype(np.float64) @ B + b) * -0.5
+    mag = (np.abs(A).astype(np.float64) @ np.abs(B) + np.abs(b)) * 0.5
+    assert np.all(np.abs(got - want) <= 1e-4 * mag + 1e-5)

@@ -36,11 +36,12 @@ def both(case, loops=None, **devkw):
     return got, o.last_received, launches
 
 
+@pytest.mark.parametrize("gemm", ["tc", "simt"])
 @pytest.mark.parametrize("case", ["unary", "unary+tetris", "dotprod", "layernorm",
                                   "lnsm_64_256", "lnsm_33_96", "lnsm_16_4096",
                                   "dotsig_128", "dotsig_256"])
-def test_parity(case):
-    got, want, n = both(case)
+def test_parity(case, gemm):
+    got, want, n = both(case, gemm=gemm)
     assert n > 0
     for g, w in zip(got, want):
         np.testing.assert_allclose(g, w, rtol=1e-4, atol=1e-5)
