@@ -325,6 +325,28 @@ class CudaB200Device:
         if flag[0] != 0:
             raise rt.ADError(f"device kernel reported error code {int(flag[0])} (bounded wait expired)")
 
+    def capture(self, cmds: Optional[List] = None) -> rt.Graph:
+        """One CUDA graph that launches every kernel of ``cmds`` (default: the
+        compute commands of the prepared main proc) in program order."""
+        rt.graph_begin(self.ctx, 0)
+        try:
+            self.replay(cmds)
+        except Exception:
+            rt.graph_end(self.ctx, 0)
+            raise
+        return rt.graph_end(self.ctx, 0)
+
+    def capture_launches(self, launches: List["Launch"], repeat: int = 1) -> rt.Graph:
+        rt.graph_begin(self.ctx, 0)
+        try:
+            for _ in range(repeat):
+                for L in launches:
+                    self._launch(L)
+        except Exception:
+            rt.graph_end(self.ctx, 0)
+            raise
+        return rt.graph_end(self.ctx, 0)
+
     def replay(self, cmds: Optional[List] = None) -> None:
         """Re-launch the compute commands of the prepared proc (no host I/O)."""
         for c in (cmds if cmds is not None else self.proc.procedure):

@@ -356,3 +356,86 @@ def plan(dev, cmd, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
     g.extra["suffix"] = [ctypes.c_uint64(dev.err_ptr)]
     g.flops = 2 * M * N * K
     return [sa, sb, g]
+
+
+# ---------------------------------------------------------------- tensor-pipe peak probe
+
+PROBE_TEMPLATE = r"""
+extern "C" __global__ void __launch_bounds__(128, 1) tf32_probe(int iters, int* __restrict__ err) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = (unsigned char*)(((unsigned long long)smem_raw + 1023) & ~1023ull);
+    unsigned long long* bar = (unsigned long long*)(smem + 3 * 32768);
+    unsigned* tmem_slot = (unsigned*)(bar + 1);
+    const int warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < 3 * 32768 / 4; i += 128) ((float*)smem)[i] = 0.0f;
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"((unsigned)__cvta_generic_to_shared(bar)));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;"
+                     :: "r"((unsigned)__cvta_generic_to_shared(tmem_slot)) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const unsigned tmem = *tmem_slot;
+    if (threadIdx.x == 0) {
+        constexpr unsigned IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((256u >> 3) << 17) | ((128u >> 4) << 24);
+        const unsigned long long base = (unsigned long long)(((unsigned)__cvta_generic_to_shared(smem)) >> 4) & 0x3FFFull;
+        const unsigned long long ad = base | (1ull << 16) | ((1024ull >> 4) << 32) | (1ull << 46) | (2ull << 61);
+        const unsigned long long bd = ad + (16384ull >> 4);
+        for (int i = 0; i < iters; ++i) {
+            const unsigned long long adv = (unsigned long long)((i & 3) * 32) >> 4;
+            asm volatile("{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+                         " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}"
+                         :: "r"(tmem), "l"(ad + adv), "l"(bd + adv), "r"(IDESC), "r"((unsigned)(i > 0)) : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                     :: "r"((unsigned)__cvta_generic_to_shared(bar)) : "memory");
+    }
+    __syncwarp();
+    unsigned ok = 0;
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    while (true) {
+        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n selp.u32 %0, 1, 0, p;\n}"
+                     : "=r"(ok) : "r"((unsigned)__cvta_generic_to_shared(bar)) : "memory");
+        if (ok) break;
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > 2000000000ull) { atomicExch(err, 4); break; }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" :: "r"(tmem) : "memory");
+}
+"""
+
+
+def measure_tf32_peak(ctx, err_ptr: int, iters: int = 4096, reps: int = 5) -> float:
+    """Dense kind::tf32 tensor-pipe throughput (TFLOP/s) with operands resident in
+    shared memory: one CTA per SM issuing back-to-back 128x256x8 MMAs."""
+    from . import runtime as rt
+    cub = rt.compile_cubin(PROBE_TEMPLATE, "tf32_probe.cu")
+    k = ctx.load(cub, "tf32_probe")
+    smem = 3 * 32768 + 2048
+    k.set_smem(smem)
+    it = ctypes.c_int(iters)
+    ep = ctypes.c_uint64(err_ptr)
+    argv = (ctypes.c_void_p * 2)(ctypes.addressof(it), ctypes.addressof(ep))
+    grid = (ctx.sm_count, 1, 1)
+    ctx.launch(k, grid, (128, 1, 1), smem, argv, 0)
+    ctx.sync()
+    e0, e1 = ctx.event(True), ctx.event(True)
+    e0.record(0)
+    for _ in range(reps):
+        ctx.launch(k, grid, (128, 1, 1), smem, argv, 0)
+    e1.record(0)
+    e1.sync()
+    ms = e0.elapsed_ms(e1) / reps
+    flops = ctx.sm_count * iters * 2.0 * 128 * 256 * 8
+    return flops / (ms / 1e3) / 1e12

@@ -140,7 +140,7 @@ def arg_ids(c) -> List[int]:
     return sorted(set(ids))
 
 
-def gen_kernel(c, name: str, faithful_tree: bool = True) -> str:
+def gen_kernel(c, name: str, faithful_tree: bool = True, dot_rows: Optional[int] = None) -> str:
     ids = arg_ids(c)
     head = "".join(f"    float *buf_{i} = B[{j}];\n" for j, i in enumerate(ids))
     kind = type(c).__name__
@@ -191,6 +191,8 @@ def gen_kernel(c, name: str, faithful_tree: bool = True) -> str:
     if kind in ("DotProdNode", "DPElwFuse"):
         dn = c if kind == "DotProdNode" else c.init_node
         m, kdim = dn.children_shapes[0]
+        if dot_rows is not None:
+            m = min(m, dot_rows)   # bounded CPU-baseline sample: first rows only
         ncol = dn.children_shapes[1][1]
         if kind == "DotProdNode":
             epi = f"{lower_karg(dn.kres)} = _value;"
@@ -246,8 +248,10 @@ def compile_kernels(srcs: Dict[str, str], flags: Optional[List[str]] = None) -> 
 class OracleDevice:
     """CPU executor with the reference device's walk (opencl/device.py:46-130)."""
 
-    def __init__(self, faithful_tree: bool = True, threads: Optional[int] = None):
+    def __init__(self, faithful_tree: bool = True, threads: Optional[int] = None,
+                 dot_rows: Optional[int] = None):
         self.faithful_tree = faithful_tree
+        self.dot_rows = dot_rows
         self.buffers: Dict[int, np.ndarray] = {}
         self.kernels = {}
         if threads is not None:
@@ -267,7 +271,7 @@ class OracleDevice:
                 self.buffers[c.id] = buf
             elif type(c).__name__ in ir.COMPUTE_KINDS:
                 name = f"k{len(srcs)}"
-                srcs[name] = gen_kernel(c, name, self.faithful_tree)
+                srcs[name] = gen_kernel(c, name, self.faithful_tree, self.dot_rows)
                 self._cmds.append((c, name))
         lib = compile_kernels(srcs) if srcs else None
         for c, name in self._cmds:
