@@ -12,7 +12,7 @@ import sys
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 LIB = os.path.join(PKG, "libad_b200.so")
-SOURCES = [os.path.join(PKG, "csrc", "runtime.cu")]
+SOURCES = [os.path.join(PKG, "csrc", "runtime.cu"), os.path.join(PKG, "csrc", "noalloc.cu")]
 HEADERS = [os.path.join(ROOT, "include", "ad_b200.h")]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 

@@ -164,6 +164,10 @@ int nccl() {
 
 }  // namespace
 
+namespace ad_b200_internal {
+void set_error(const char* msg) { g_err = msg; }
+}  // namespace ad_b200_internal
+
 // ---------------------------------------------------------------- objects
 struct ad_ctx {
   int device = 0;

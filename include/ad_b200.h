@@ -114,6 +114,20 @@ int ad_allreduce_f32(ad_ctx* ctx, uint64_t send, uint64_t recv, size_t count, in
                      int stream);
 int ad_nccl_abort(ad_ctx* ctx);
 
+/* C = A @ B (b_is_nk = 0: B is K x N row-major) or C = A @ B^T (b_is_nk = 1:
+ * B is N x K row-major); A is M x K row-major, C is M x N row-major, all fp32
+ * device pointers; 3xTF32 on tcgen05.  No counterpart in the reference: this
+ * entry point exists for callers that cannot allocate device memory.  It
+ * allocates nothing: its split-operand scratch is a fixed 32 MiB device array
+ * inside this library, so problems needing more than 8*(Mp+Np)*Kp + 256 bytes
+ * of it (Mp = M rounded up to 128, Np = N to 256, Kp = K to 32) are rejected.
+ * All calls share that array: calls that overlap on one GPU race.  The first
+ * call on each device resolves the array's address (cudaGetSymbolAddress), so
+ * make it before any stream capture.  `stream` is a cudaStream_t (NULL = the
+ * legacy default stream); the call returns after its work has finished. */
+int ad_dot_tf32x3_noalloc(const float* A, const float* B, float* C, int M, int N, int K,
+                          int b_is_nk, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,35 @@
+"""The C-ABI library loads without a GPU and exports every symbol its header declares."""
+import ctypes
+import os
+import re
+
+from ad_b200 import runtime as rt
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared():
+    src = open(os.path.join(ROOT, "include", "ad_b200.h")).read()
+    return sorted(set(re.findall(r"^(?:int|void|const char\*)\s+(ad_\w+)\s*\(", src, re.M)))
+
+
+def test_exports_every_declared_symbol():
+    L = rt.lib()
+    names = declared()
+    assert len(names) >= 30
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(rt.SIGNATURES), set(names) ^ set(rt.SIGNATURES)
+
+
+def test_version_and_errors_without_gpu():
+    L = rt.lib()
+    assert L.ad_version() == 1
+    # a call that must fail cleanly (null context) reports a message
+    assert L.ad_stream_sync(None, 0) != 0
+    assert b"null context" in L.ad_last_error()
+
+
+def test_nvrtc_compiles_sm100a():
+    cub = rt.compile_cubin('extern "C" __global__ void k(float* p) { p[threadIdx.x] = 1.0f; }', "t.cu")
+    assert len(cub) > 100
