@@ -63,8 +63,9 @@ class CudaB200Device:
     """Device plug-in with the reference's interface (device/__init__.py:1-6)."""
 
     def __init__(self, device: int = 0, use_graphs: bool = True, gemm: str = "auto",
-                 verbose: bool = False, comm=None):
+                 verbose: bool = False, comm=None, rowfuse: bool = True):
         self.ctx = rt.Context(device)
+        self.rowfuse = rowfuse and os.environ.get("AD_ROWFUSE", "1") != "0"
         self.use_graphs = use_graphs and os.environ.get("AD_GRAPH", "1") != "0"
         self.gemm = os.environ.get("AD_GEMM", gemm)
         self.verbose = verbose
@@ -121,6 +122,11 @@ class CudaB200Device:
         if kind in DOT:
             from . import gemm
             return gemm.plan_dot(self, cmd, name, sizes)
+        if kind == "RowFused":
+            from . import rowfuse
+            spec = rowfuse.gen_rowfused(cmd, "k_RowFused", sizes, self.ctx.sm_count)
+            spec.extra["suffix"] = [ctypes.c_uint64(self.err_ptr)]
+            return [spec]
         raise TypeError(f"Encountered unexpected cmd: {kind}")
 
     def init(self, cmd) -> None:
@@ -293,7 +299,10 @@ class CudaB200Device:
     # ------------------------------------------------------------ entry point
     def prepare(self, proc) -> ir.Proc:
         """Init pass: plan + allocate memory, upload contents, build all kernels."""
-        proc = ir.conv_proc(proc)
+        proc = ir.copy_structure(ir.conv_proc(proc))
+        if self.rowfuse:
+            from . import rowfuse
+            rowfuse.fuse_rows(proc)
         self.proc = proc
         self._pinned_ptrs: List[int] = []
         self._setup_memory(proc)
@@ -350,7 +359,7 @@ class CudaB200Device:
     def replay(self, cmds: Optional[List] = None) -> None:
         """Re-launch the compute commands of the prepared proc (no host I/O)."""
         for c in (cmds if cmds is not None else self.proc.procedure):
-            if type(c).__name__ in ir.COMPUTE_KINDS:
+            if id(c) in self.launches:
                 self.run(c)
 
     def close(self) -> None:

@@ -43,6 +43,9 @@ def load_case(case: str, path: Optional[str] = None, with_content: bool = True):
             if f is not None and "fill" in f:
                 val, shape = f["fill"], tuple(f["shape"])
                 c.func = lambda val=val, shape=shape: np.full(shape, val, dtype=np.float32)
+            elif f is not None and "spec" in f:
+                arr = make_array(f["spec"])
+                c.func = lambda arr=arr: arr
     return proc, meta
 
 

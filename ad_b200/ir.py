@@ -317,7 +317,7 @@ class ForNode:
 
 
 COMPUTE_KINDS = ("BinaryNode", "UnaryNode", "ContigiousNode", "ReduceNode",
-                 "DotProdNode", "ElwFuse", "ReduceElwFuse", "DPElwFuse")
+                 "DotProdNode", "ElwFuse", "ReduceElwFuse", "DPElwFuse", "RowFused")
 
 # --------------------------------------------------------------------------
 # Conversion from the reference's live objects (duck-typed by class name)
@@ -410,6 +410,18 @@ def conv_cmd(c):
         cls = {"ElwFuse": ElwFuse, "ReduceElwFuse": ReduceElwFuse, "DPElwFuse": DPElwFuse}[n]
         return cls(nodes, init, pid, int(getattr(c, "fuse_id", -1)))
     raise TypeError(f"unsupported proc entry {n}")
+
+
+def copy_structure(p: Proc) -> Proc:
+    """A new Proc (and new ForNode/Proc containers) sharing the commands, so that
+    device-side rewrites of the command list never touch the caller's proc."""
+    out = []
+    for c in p.procedure:
+        if isinstance(c, ForNode):
+            out.append(ForNode(c.id, copy_structure(c.proc), c.r))
+        else:
+            out.append(c)
+    return Proc(out, p.id)
 
 
 def conv_proc(p) -> Proc:

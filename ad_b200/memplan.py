@@ -50,6 +50,8 @@ class Slot:
 def _accesses(c) -> Tuple[List[int], List[int]]:
     """(reads, writes) buffer ids of one command."""
     kind = type(c).__name__
+    if hasattr(c, "accesses"):
+        return c.accesses()
     if kind == "Feeder":
         return [], c.kres.ids(True)
     if kind == "Receiver":
@@ -124,6 +126,8 @@ def plan(proc: ir.Proc) -> Tuple[Dict[int, Slot], int]:
     end_all = pos[0] + 1
     slots: Dict[int, Slot] = {}
     for b, n in sizes.items():
+        if not content.get(b) and b not in first:
+            continue   # never touched by a launch or a host copy (e.g. kept in registers)
         if content.get(b) or b not in first:
             s, e = 0, end_all
         else:

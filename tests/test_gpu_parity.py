@@ -36,15 +36,25 @@ def both(case, loops=None, **devkw):
     return got, o.last_received, launches
 
 
-@pytest.mark.parametrize("gemm", ["tc", "simt"])
+@pytest.mark.parametrize("gemm,rowfuse", [("tc", True), ("simt", True), ("tc", False)])
 @pytest.mark.parametrize("case", ["unary", "unary+tetris", "dotprod", "layernorm",
                                   "lnsm_64_256", "lnsm_33_96", "lnsm_16_4096",
-                                  "dotsig_128", "dotsig_256"])
-def test_parity(case, gemm):
-    got, want, n = both(case, gemm=gemm)
+                                  "dotsig_128", "dotsig_256", "enc_1_2_16_32_2_64_3"])
+def test_parity(case, gemm, rowfuse):
+    got, want, n = both(case, gemm=gemm, rowfuse=rowfuse)
     assert n > 0
     for g, w in zip(got, want):
         np.testing.assert_allclose(g, w, rtol=1e-4, atol=1e-5)
+
+
+def test_rowfuse_collapses_lnsm():
+    from ad_b200.device import CudaB200Device
+    p, _ = load_case("lnsm_16_4096")
+    d = CudaB200Device()
+    d.prepare(p)
+    kinds = [L.spec.kind for ls in d.launches.values() for L in ls]
+    d.close()
+    assert kinds == ["rowfused"]
 
 
 @pytest.mark.parametrize("case", ["powtwo", "variance", "concat"])
