@@ -654,3 +654,39 @@ def gen_dot_simt(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
     rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
     return KernelSpec(name, src, bufs, grid, (256, 1, 1), 0, "dot_simt",
                       written_reads_bytes(c, rngw, sizes), 2 * M * N * K)
+
+
+def gen_dot_warp(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
+    """Skinny dot products (few outputs, long K: e.g. the batch-2 MLP of
+    examples/linear.py): one warp per output element, lanes stride over K,
+    shuffle reduction, lane 0 runs the fused epilogue."""
+    dn, M, N, K = dot_shape(c)
+    bufs = cmd_buffers(c)
+    rng = {"X": (0, max(M, K) - 1), "Y": (0, max(N, K) - 1), "G": (0, M * N - 1)}
+    it = index_type(c, rng)
+    em = Emitter(bufs, it)
+    A, B = dn.kargs
+    la = em.scalar_karg(A, {"X": "om", "Y": "kk"}, {})
+    lb = em.scalar_karg(B, {"X": "kk", "Y": "on"}, {})
+    epi = dot_epilogue(c, em, it, "accv", {"X": "om", "Y": "on", "G": f"(om * ({it}){N} + on)"})
+    epi = "\n            ".join(epi.split("\n"))
+    params = ", ".join(f"float* __restrict__ p{i}" for i in range(len(bufs)))
+    src = f"""extern "C" __global__ void __launch_bounds__(256) {name}({params}) {{
+    const long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (w >= {M * N}LL) return;
+    const {it} om = ({it})(w / {N}), on = ({it})(w % {N});
+    float acc = 0.0f;
+    for ({it} kk = lane; kk < ({it}){K}; kk += 32) acc = fmaf({la}, {lb}, acc);
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {{
+            const float accv = acc;
+            {epi}
+    }}
+}}
+"""
+    grid = ((M * N + 7) // 8, 1, 1)
+    rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
+    return KernelSpec(name, src, bufs, grid, (256, 1, 1), 0, "dot_warp",
+                      written_reads_bytes(c, rngw, sizes), 2 * M * N * K)

@@ -225,23 +225,14 @@ class CudaB200Device:
                 func(cmd)
 
     # ------------------------------------------------------------ graphs
-    def _capture(self, body: ir.Proc, staging: Dict[int, np.ndarray]):
-        """Capture one replay of ``body`` (no Receivers) into a CUDA graph.
-        Feeder copies read from ``staging`` (pinned host arrays)."""
+    def _capture(self, body: ir.Proc, stagings: List[Dict[int, np.ndarray]]):
+        """Capture ``len(stagings)`` consecutive replays of ``body`` (no Receivers)
+        into one CUDA graph; replay i's Feeder copies read ``stagings[i]``
+        (pinned host arrays)."""
         rt.graph_begin(self.ctx, 0)
         try:
-            for cmd in body.procedure:
-                kind = type(cmd).__name__
-                if kind == "Feeder":
-                    a = staging[id(cmd)]
-                    self.ctx.h2d(self.ptr(cmd.kres.id) + 4 * offset_of(cmd.kres), a.ctypes.data, a.nbytes, 0)
-                elif kind in ("AllocEntry", "DeallocEntry"):
-                    continue
-                elif kind == "ForNode":
-                    for _ in cmd.r:
-                        self._capture_inline(cmd.proc, staging)
-                else:
-                    self.run(cmd)
+            for staging in stagings:
+                self._capture_inline(body, staging)
         except Exception:
             try:
                 rt.graph_end(self.ctx, 0)
@@ -268,30 +259,43 @@ class CudaB200Device:
         self._pinned_ptrs.append(p.value)
         return np.ctypeslib.as_array((ctypes.c_float * (nbytes // 4)).from_address(p.value))
 
-    def _replay_graph(self, loop: ir.ForNode) -> None:
-        feeders = [c for c in ir.iter_cmds(loop.proc) if type(c).__name__ == "Feeder"]
-        key = id(loop)
+    LOOP_UNROLL = 16
+
+    def _loop_graphs(self, loop: ir.ForNode, feeders, u: int):
+        """Two graphs (ping-pong) of ``u`` iterations each, with their own pinned
+        Feeder staging, so the host fills one while the GPU runs the other."""
+        key = (id(loop), u)
         if key not in self._graphs:
             pairs = []
             for _ in range(2 if feeders else 1):
-                staging = {id(f): self._pinned(4 * math.prod(f.shape)) for f in feeders}
-                g = self._capture(loop.proc, staging)
-                done = self.ctx.event(False)
-                pairs.append((g, staging, done, [False]))
+                stagings = [{id(f): self._pinned(4 * math.prod(f.shape)) for f in feeders} for _ in range(u)]
+                g = self._capture(loop.proc, stagings)
+                pairs.append((g, stagings, self.ctx.event(False), [False]))
             self._graphs[key] = pairs
-        pairs = self._graphs[key]
+        return self._graphs[key]
+
+    def _replay_graph(self, loop: ir.ForNode) -> None:
+        """Run ``len(loop.r)`` iterations as launches of graphs that each hold
+        LOOP_UNROLL iterations.  Feeder functions are still called once per
+        iteration, in order, before the graph that consumes their data."""
+        feeders = [c for c in ir.iter_cmds(loop.proc) if type(c).__name__ == "Feeder"]
+        n = len(loop.r)
+        u = max(1, min(n, self.LOOP_UNROLL))
+        chunks = [u] * (n // u) + ([n % u] if n % u else [])
         n_kern = sum(len(self.launches.get(id(c), [])) for c in ir.iter_cmds(loop.proc))
-        for i in range(len(loop.r)):
-            g, staging, done, used = pairs[i % len(pairs)]
+        for ci, cu in enumerate(chunks):
+            pairs = self._loop_graphs(loop, feeders, cu)
+            g, stagings, done, used = pairs[ci % len(pairs)]
             if feeders:
                 if used[0]:
-                    done.sync()  # the copy that read this staging slot has finished
-                for f in feeders:
-                    arr = f.func()
-                    assert isinstance(arr, np.ndarray) and list(arr.shape) == list(f.shape), "Invalid function"
-                    staging[id(f)][:] = np.asarray(arr, dtype=np.float32).reshape(-1)
+                    done.sync()  # the copies that read these staging slots have finished
+                for i in range(cu):
+                    for f in feeders:
+                        arr = f.func()
+                        assert isinstance(arr, np.ndarray) and list(arr.shape) == list(f.shape), "Invalid function"
+                        stagings[i][id(f)][:] = np.asarray(arr, dtype=np.float32).reshape(-1)
             g.launch(0)
-            self.n_launches += n_kern
+            self.n_launches += n_kern * cu
             if feeders:
                 done.record(0)
                 used[0] = True
@@ -393,7 +397,14 @@ class CudaB200Device:
 
 
 def graphable(p: ir.Proc) -> bool:
-    return not any(type(c).__name__ == "Receiver" for c in ir.iter_cmds(p))
+    """A loop body can be replayed as a graph if it has no Receiver (host callback)
+    and no nested loop that feeds host data."""
+    if any(type(c).__name__ == "Receiver" for c in ir.iter_cmds(p)):
+        return False
+    for c in p.procedure:
+        if isinstance(c, ir.ForNode) and any(type(x).__name__ == "Feeder" for x in ir.iter_cmds(c.proc)):
+            return False
+    return True
 
 
 def offset_of(k) -> int:

@@ -5,8 +5,10 @@ one output per work item (opencl/kernels/dotprod.py:7-43) and runs the fused
 epilogue with ``_x = ty, _y = tx, _global_id = ty * wB + tx``
 (opencl/kernels/dp_elw_fuse.py:11-65).  This module picks the B200 schedule:
 
-* ``simt``: fp32 CUDA-core tiles (``codegen.gen_dot_simt``), for tiny
-  products where a tensor-core tile would be mostly padding.
+* ``simt``: fp32 CUDA-core kernels for tiny products where a tensor-core
+  tile would be mostly padding: one warp per output for few outputs with a
+  long K (``codegen.gen_dot_warp``), 64x64 register tiles otherwise
+  (``codegen.gen_dot_simt``).
 * ``tc``: tcgen05 tensor cores with 3xTF32 (see ``tcgen05.py``).
 """
 from __future__ import annotations
@@ -30,6 +32,8 @@ def plan_dot(dev, cmd, name: str, sizes: Dict[int, int]) -> List[codegen.KernelS
     if use_tensor_cores(dev, M, N, K):
         from . import tcgen05
         return tcgen05.plan(dev, cmd, name, sizes)
+    if K >= 32 and M * N <= 32768:
+        return [codegen.gen_dot_warp(cmd, name + "_warp", sizes)]
     return [codegen.gen_dot_simt(cmd, name + "_simt", sizes)]
 
 

@@ -444,6 +444,16 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
             decl.append(f"float s{b} = 0.0f;")
 
     defined: Set = set()   # (buffer, chunk) for row buffers, buffer for scalars: value is in registers
+    staged_loaded: Set = set()
+
+    def staged_reg(b: int, k: int) -> str:
+        """The row's chunk k of staged input b, read from shared memory once per row."""
+        name_ = f"c{b}_{k}"
+        if (b, k) not in staged_loaded:
+            staged_loaded.add((b, k))
+            decl.append(f"float4 {name_};")
+            lines.append(f"{name_} = stg[(slot * {len(staged)} + {sidx[b]}) * {U} + {k} * {gs} + tig];")
+        return name_
 
     def gbase(k: int) -> str:
         return f"(rowbase + ((({it}){k} * {gs} + tig) * {VEC}))"
@@ -472,9 +482,7 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
                         out.append(sc_regs[karg.id])
                     return
                 if karg.id in sidx:
-                    q = em.tmp("q")
-                    lines.append(f"const float4 {q} = stg[(slot * {len(staged)} + {sidx[karg.id]}) * {U} + "
-                                 f"{k} * {gs} + tig];")
+                    q = staged_reg(karg.id, k)
                     out.extend(f"{q}.{cmp}" for cmp in "xyzw")
                     return
                 ln = exprs.lanes(karg.access, "G", VEC)
@@ -567,25 +575,42 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
             if b not in rf.internal:
                 lines.append(f"if (live && tig == 0) {em.p(b)}[{em.expr(n.kres.access, env)}] = {tv};")
 
-    n_red = 0
+    # consecutive reductions are independent of each other (a reduction reads a full
+    # row buffer and writes per-row scalars), so a group of them shares one
+    # shared-memory exchange and one barrier; their epilogues then run in order.
+    groups: List[List] = []
     for c in rf.cmds:
         ck = _cmd_kind(c, V, R)
+        if ck == "reduce" and groups and groups[-1][0] == "reduce":
+            groups[-1][1].append(c)
+        else:
+            groups.append([ck, [c]])
+    max_group = max([len(g[1]) for g in groups if g[0] == "reduce"] or [1])
+    n_red = 0
+    for ck, members in groups:
         if ck == "full":
+            c = members[0]
             for k in range(nc):
                 lines.append(f"{{ // chunk {k}")
                 emit_full(c, k)
                 lines.append("}")
-        elif ck == "scalar":
+            continue
+        if ck == "scalar":
             lines.append("{")
-            emit_scalar_chain(codegen.chain_nodes(c))
+            emit_scalar_chain(codegen.chain_nodes(members[0]))
             lines.append("}")
-        else:
+            continue
+        accs = []
+        combs = []
+        for c in members:
             rn = c if type(c).__name__ == "ReduceNode" else c.init_node
             op = rn.op
             ident = "0.0f" if op == "SUM" else "(__int_as_float(0xff800000))"
             comb = (lambda a, b: f"({a} + {b})") if op == "SUM" else (lambda a, b: f"fmaxf({a}, {b})")
             src = rn.kargs[0]
             acc = em.tmp("acc")
+            accs.append(acc)
+            combs.append(comb)
             lines.append(f"float {acc} = {ident};")
             for k in range(nc):
                 env0 = {"X": "xr", "Y": f"((({it}){k} * {gs} + tig) * {VEC})", "G": "xr"}
@@ -593,9 +618,7 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
                     vs = row_regs[src.id][k]
                     lines.append(f"{acc} = {comb(acc, comb(comb(vs[0], vs[1]), comb(vs[2], vs[3])))};")
                 elif isinstance(src, ir.KMatrix) and not src.is_temp and src.id in sidx:
-                    q = em.tmp("q")
-                    lines.append(f"const float4 {q} = stg[(slot * {len(staged)} + {sidx[src.id]}) * {U} + "
-                                 f"{k} * {gs} + tig];")
+                    q = staged_reg(src.id, k)
                     lines.append(f"{acc} = {comb(acc, comb(comb(q + '.x', q + '.y'), comb(q + '.z', q + '.w')))};")
                 elif isinstance(src, ir.KConstant):
                     lines.append(f"{acc} = {comb(acc, flit(src.constant))};" if op == "MAX" else
@@ -611,23 +634,28 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
                         for j in range(VEC):
                             envj = {"X": "xr", "Y": f"(((({it}){k} * {gs} + tig) * {VEC}) + {j})", "G": "xr"}
                             lines.append(f"if (live) {acc} = {comb(acc, em.scalar_karg(src, envj, {}))};")
-            # group reduction, result broadcast to all threads of the row group
-            w = min(gs, 32)
-            lines.append(f"#pragma unroll\nfor (int o = {w // 2}; o > 0; o >>= 1) {acc} = "
-                         f"{comb(acc, f'__shfl_xor_sync(0xffffffffu, {acc}, o)')};")
-            if gs > 32:
-                nw = gs // 32
-                lines.append(f"if ((threadIdx.x & 31) == 0) red[{n_red % 2}][threadIdx.x >> 5] = {acc};")
-                lines.append("__syncthreads();")
-                parts = [f"red[{n_red % 2}][grp * {nw} + {i}]" for i in range(nw)]
+        # group reduction, results broadcast to all threads of the row group
+        w = min(gs, 32)
+        lines.append(f"#pragma unroll\nfor (int o = {w // 2}; o > 0; o >>= 1) {{")
+        for acc, comb in zip(accs, combs):
+            lines.append(f"    {acc} = {comb(acc, f'__shfl_xor_sync(0xffffffffu, {acc}, o)')};")
+        lines.append("}")
+        if gs > 32:
+            nw = gs // 32
+            slot_r = n_red % 2
+            for ai, acc in enumerate(accs):
+                lines.append(f"if ((threadIdx.x & 31) == 0) red[{slot_r}][{ai}][threadIdx.x >> 5] = {acc};")
+            lines.append("__syncthreads();")
+            for ai, (acc, comb) in enumerate(zip(accs, combs)):
+                parts = [f"red[{slot_r}][{ai}][grp * {nw} + {i}]" for i in range(nw)]
                 tot = parts[0]
                 for pp in parts[1:]:
                     tot = comb(tot, pp)
                 lines.append(f"{acc} = {tot};")
-            n_red += 1
-            nodes = codegen.chain_nodes(c)
+        n_red += 1
+        for c, acc in zip(members, accs):
             lines.append("{")
-            emit_scalar_chain(nodes, acc)
+            emit_scalar_chain(codegen.chain_nodes(c), acc)
             lines.append("}")
     params = ", ".join([f"float* __restrict__ p{i}" for i in range(len(bufs))] + ["int* __restrict__ err"])
     nw_tot = max(1, block // 32)
@@ -635,7 +663,7 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
     if not staged_mode:
         body = "\n    ".join(body_lines)
         src = f"""extern "C" __global__ void __launch_bounds__({block}) {name}({params}) {{
-    __shared__ float red[2][{nw_tot}];
+    __shared__ float red[2][{max_group}][{nw_tot}];
     const int tig = threadIdx.x % {gs};
     const int grp = threadIdx.x / {gs};
     (void)grp; (void)red; (void)err;
@@ -678,7 +706,7 @@ __device__ __noinline__ bool rf_wait(unsigned long long* b, unsigned ph) {{
 
 extern "C" __global__ void __launch_bounds__({block}) {name}({params}) {{
     extern __shared__ __align__(128) float4 stg[];
-    __shared__ float red[2][{nw_tot}];
+    __shared__ float red[2][{max_group}][{nw_tot}];
     __shared__ __align__(8) unsigned long long bar[2];
     const int tig = threadIdx.x;
     const int grp = 0;

@@ -120,7 +120,7 @@ def _karg_exprs(k):
 GEMM_TEMPLATE = r"""
 struct __align__(64) TmapT { unsigned long long v[16]; };
 
-#define AD_WAIT_NS 2000000000ull   // 2 s: far above any legitimate wait of one tile
+#define AD_WAIT_NS 2000000000ull   // 2 s: far above any legitimate wait
 
 __device__ __forceinline__ unsigned smem_u32(const void* p) {
     return (unsigned)__cvta_generic_to_shared(p);
@@ -139,15 +139,19 @@ __device__ __forceinline__ unsigned long long gtime() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// bounded wait on an mbarrier phase: false after AD_WAIT_NS without completion
-__device__ __noinline__ bool mbar_wait(unsigned long long* b, unsigned phase) {
+// bounded wait on an mbarrier phase: false after AD_WAIT_NS, or at once if another role aborted
+__device__ __noinline__ bool mbar_wait(unsigned long long* b, unsigned phase, volatile int* abort_flag) {
     if (mbar_try(b, phase)) return true;
     const unsigned long long t0 = gtime();
     while (true) {
-        for (int i = 0; i < 256; ++i)
+        for (int i = 0; i < 128; ++i)
             if (mbar_try(b, phase)) return true;
+        if (*abort_flag) return false;
         if (gtime() - t0 > AD_WAIT_NS) return false;
     }
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(b)) : "memory");
 }
 __device__ __forceinline__ void mbar_expect_tx(unsigned long long* b, unsigned bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(b)), "r"(bytes) : "memory");
@@ -169,30 +173,46 @@ __device__ __forceinline__ void mma_tf32(unsigned tmem, unsigned long long ad, u
 __device__ __forceinline__ void mma_commit(unsigned long long* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void tile_of(int t, int& m_blk, int& n_blk) {
+    // grouped raster: GROUP m-blocks share each sweep over n so A panels stay in L2
+    constexpr int GROUP = 8, NUM_M = M_BLOCKS, NUM_N = N_BLOCKS;
+    const int per_group = GROUP * NUM_N;
+    const int g = t / per_group, first = g * GROUP;
+    const int gsz = (NUM_M - first) < GROUP ? (NUM_M - first) : GROUP;
+    const int r = t % per_group;
+    m_blk = first + r % gsz;
+    n_blk = r / gsz;
+}
 
-extern "C" __global__ void __launch_bounds__(128, 1) NAME(
+// Persistent, warp-specialised: warp 0 = TMA producer, warp 1 = MMA issuer,
+// warps 2..9 = epilogue (TMEM lane quarter = warp % 4, column half = (warp - 2) / 4).
+// Two TMEM accumulators (2 x BN columns) let the epilogue of one tile overlap the
+// MMAs of the next.
+extern "C" __global__ void __launch_bounds__(320, 1) NAME(
     const __grid_constant__ TmapT tAh, const __grid_constant__ TmapT tAl,
     const __grid_constant__ TmapT tBh, const __grid_constant__ TmapT tBl,
     PARAMS int* __restrict__ err)
 {
-    constexpr int BN = TILE_N, STAGES = NSTAGES, KB = KBLOCKS;
+    constexpr int BN = TILE_N, STAGES = NSTAGES, KB = KBLOCKS, NUM_TILES = M_BLOCKS * N_BLOCKS;
     constexpr unsigned A_BYTES = 128 * 128, B_BYTES = BN * 128;
     constexpr unsigned STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    constexpr int EPI_WARPS = 8;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = (unsigned char*)(((unsigned long long)smem_raw + 1023) & ~1023ull);
-    unsigned long long* full = (unsigned long long*)(smem + STAGES * STAGE_BYTES);
+    float* trans = (float*)(smem + STAGES * STAGE_BYTES);                     // 8 warps x 32 x 32
+    unsigned long long* full = (unsigned long long*)(trans + EPI_WARPS * 1024);
     unsigned long long* empty = full + STAGES;
-    unsigned long long* accb = empty + STAGES;
-    unsigned* tmem_slot = (unsigned*)(accb + 1);
+    unsigned long long* tfull = empty + STAGES;
+    unsigned long long* tempty = tfull + 2;
+    unsigned* tmem_slot = (unsigned*)(tempty + 2);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
     volatile int* consumed = abort_flag + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * 128, n0 = blockIdx.x * BN;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        mbar_init(accb, 1);
+        for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], EPI_WARPS); }
         *abort_flag = 0;
         *consumed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -200,7 +220,7 @@ extern "C" __global__ void __launch_bounds__(128, 1) NAME(
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     :: "r"(smem_u32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+                     :: "r"(smem_u32(tmem_slot)), "r"(2 * BN) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -208,98 +228,142 @@ extern "C" __global__ void __launch_bounds__(128, 1) NAME(
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const unsigned tmem = *tmem_slot;
 
-    if (warp == 0 && lane == 0) {
-        // TMA producer
-        int issued = 0;
-        for (int kb = 0; kb < KB; ++kb) {
-            const int s = kb % STAGES;
-            if (kb >= STAGES) {
-                if (!mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { *abort_flag = 1; atomicExch(err, 1); break; }
-            }
-            if (*abort_flag) break;
-            unsigned char* st = smem + s * STAGE_BYTES;
-            mbar_expect_tx(&full[s], STAGE_BYTES);
-            tma_load_2d(st, &tAh, &full[s], kb * 32, m0);
-            tma_load_2d(st + A_BYTES, &tAl, &full[s], kb * 32, m0);
-            tma_load_2d(st + 2 * A_BYTES, &tBh, &full[s], kb * 32, n0);
-            tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tBl, &full[s], kb * 32, n0);
-            issued = kb + 1;
-        }
-        if (*abort_flag) {
-            // drain: wait (bounded) for the copies this CTA issued but nobody consumed
-            for (int kb = *consumed; kb < issued; ++kb) mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1);
-        }
-    } else if (warp == 1 && lane == 0) {
-        // MMA issuer: D(128 x BN) += A(128 x 8) * B(BN x 8)^T per instruction, both K-major
-        constexpr unsigned IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((unsigned)(BN >> 3) << 17) | ((128u >> 4) << 24);
-        for (int kb = 0; kb < KB; ++kb) {
-            const int s = kb % STAGES;
-            if (!mbar_wait(&full[s], (kb / STAGES) & 1)) { *abort_flag = 1; atomicExch(err, 2); break; }
-            if (*abort_flag) break;
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            unsigned char* st = smem + s * STAGE_BYTES;
-            const unsigned long long ah = sdesc(st), al = sdesc(st + A_BYTES);
-            const unsigned long long bh = sdesc(st + 2 * A_BYTES), bl = sdesc(st + 2 * A_BYTES + B_BYTES);
-            #pragma unroll
-            for (int k8 = 0; k8 < 4; ++k8) {
-                const unsigned long long adv = (unsigned long long)(k8 * 32) >> 4;  // 8 fp32 = 32 bytes
-                const unsigned first = (kb > 0 || k8 > 0) ? 1u : 0u;
-                mma_tf32(tmem, ah + adv, bh + adv, IDESC, first);
-                mma_tf32(tmem, ah + adv, bl + adv, IDESC, 1u);
-                mma_tf32(tmem, al + adv, bh + adv, IDESC, 1u);
-            }
-            mma_commit(&empty[s]);
-            *consumed = kb + 1;
-        }
-        mma_commit(accb);
-    }
-    __syncwarp();
-
-    // ---- epilogue: all 4 warps; warp w owns TMEM lanes (rows) 32w .. 32w+31
-    bool ok = mbar_wait(accb, 0);
-    if (!ok) { atomicExch(err, 3); }
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    __syncthreads();
-    if (ok && !*abort_flag) {
-        float* tr = (float*)smem + warp * (32 * 33);   // stage memory is free now
-        #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-            unsigned r[32];
-            const unsigned taddr = tmem + ((unsigned)(warp * 32) << 16) + (unsigned)(c * 32);
-            asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-                "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                  "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-                  "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-                  "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-                : "r"(taddr));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            #pragma unroll
-            for (int j = 0; j < 32; ++j) tr[lane * 33 + j] = __uint_as_float(r[j]);
-            __syncwarp();
-            #pragma unroll 4
-            for (int i = 0; i < 32; ++i) {
-                const IDX om = (IDX)m0 + warp * 32 + i;
-                const IDX on = (IDX)n0 + c * 32 + lane;
-                if (om < (IDX)M_DIM && on < (IDX)N_DIM) {
-                    const float accv = tr[i * 33 + lane];
-                    EPILOGUE
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer
+            int it = 0;
+            for (int t = blockIdx.x; t < NUM_TILES && !*abort_flag; t += gridDim.x) {
+                int mb, nb;
+                tile_of(t, mb, nb);
+                for (int kb = 0; kb < KB; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, abort_flag)) {
+                        if (!*abort_flag) atomicExch(err, 1);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    unsigned char* st = smem + s * STAGE_BYTES;
+                    mbar_expect_tx(&full[s], STAGE_BYTES);
+                    tma_load_2d(st, &tAh, &full[s], kb * 32, mb * 128);
+                    tma_load_2d(st + A_BYTES, &tAl, &full[s], kb * 32, mb * 128);
+                    tma_load_2d(st + 2 * A_BYTES, &tBh, &full[s], kb * 32, nb * BN);
+                    tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tBl, &full[s], kb * 32, nb * BN);
                 }
             }
-            __syncwarp();
+            if (*abort_flag) {
+                // drain (bounded): copies issued but never consumed must land before exit
+                for (int k = *consumed; k < it; ++k) {
+                    const unsigned long long t0 = gtime();
+                    while (!mbar_try(&full[k % STAGES], (k / STAGES) & 1) && gtime() - t0 < AD_WAIT_NS) {}
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer: D(128 x BN) += A(128 x 8) * B(BN x 8)^T, K-major, 3xTF32
+            constexpr unsigned IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((unsigned)(BN >> 3) << 17) | ((128u >> 4) << 24);
+            int it = 0, lt = 0;
+            for (int t = blockIdx.x; t < NUM_TILES && !*abort_flag; t += gridDim.x, ++lt) {
+                const int a = lt & 1;
+                if (lt >= 2 && !mbar_wait(&tempty[a], ((lt >> 1) - 1) & 1, abort_flag)) {
+                    if (!*abort_flag) atomicExch(err, 4);
+                    *abort_flag = 1;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const unsigned d = tmem + (unsigned)(a * BN);
+                bool ok = true;
+                for (int kb = 0; kb < KB; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) {
+                        if (!*abort_flag) atomicExch(err, 2);
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    unsigned char* st = smem + s * STAGE_BYTES;
+                    const unsigned long long ah = sdesc(st), al = sdesc(st + A_BYTES);
+                    const unsigned long long bh = sdesc(st + 2 * A_BYTES), bl = sdesc(st + 2 * A_BYTES + B_BYTES);
+                    #pragma unroll
+                    for (int k8 = 0; k8 < 4; ++k8) {
+                        const unsigned long long adv = (unsigned long long)(k8 * 32) >> 4;  // 8 fp32 = 32 bytes
+                        const unsigned first = (kb > 0 || k8 > 0) ? 1u : 0u;
+                        mma_tf32(d, ah + adv, bh + adv, IDESC, first);
+                        mma_tf32(d, ah + adv, bl + adv, IDESC, 1u);
+                        mma_tf32(d, al + adv, bh + adv, IDESC, 1u);
+                    }
+                    mma_commit(&empty[s]);
+                    *consumed = it + 1;
+                }
+                if (!ok) break;
+                mma_commit(&tfull[a]);
+            }
+        }
+    } else {
+        // ---------------- epilogue warps
+        const int q = warp & 3;                 // TMEM lane quarter this warp may access
+        const int half = (warp - 2) >> 2;       // which half of the BN columns
+        float* tr = trans + (warp - 2) * 1024;
+        int lt = 0;
+        for (int t = blockIdx.x; t < NUM_TILES; t += gridDim.x, ++lt) {
+            const int a = lt & 1;
+            if (!mbar_wait(&tfull[a], (lt >> 1) & 1, abort_flag)) {
+                if (lane == 0 && !*abort_flag) atomicExch(err, 3);
+                *abort_flag = 1;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            int mb, nb;
+            tile_of(t, mb, nb);
+            const int m0 = mb * 128, n0 = nb * BN;
+            #pragma unroll 1
+            for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+                unsigned r[32];
+                const unsigned taddr = tmem + ((unsigned)(q * 32) << 16) + (unsigned)(a * BN + c * 32);
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                    "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                      "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+                      "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                      "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (c == (half + 1) * (BN / 64) - 1) {
+                    // last TMEM read of this tile by this warp: hand the accumulator back
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[a]);
+                }
+                #pragma unroll
+                for (int j = 0; j < 32; ++j) tr[lane * 32 + (j ^ lane)] = __uint_as_float(r[j]);
+                __syncwarp();
+                #pragma unroll 4
+                for (int i = 0; i < 32; ++i) {
+                    const IDX om = (IDX)m0 + q * 32 + i;
+                    const IDX on = (IDX)n0 + c * 32 + lane;
+                    if (om < (IDX)M_DIM && on < (IDX)N_DIM) {
+                        const float accv = tr[i * 32 + (lane ^ i)];
+                        EPILOGUE
+                    }
+                }
+                __syncwarp();
+            }
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0) {
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TMEM_COLS) : "memory");
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(2 * BN) : "memory");
     }
 }
 """
 
 
-def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int) -> KernelSpec:
+def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int, sm_count: int = 148) -> KernelSpec:
     bufs = cmd_buffers(c)
     rng = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
     it = index_type(_epi_only(c), rng)
@@ -308,15 +372,17 @@ def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int) -> Kern
     epi = "\n                    ".join(epi.split("\n"))
     params = "".join(f"float* __restrict__ p{i}, " for i in range(len(bufs)))
     kb = pad(K, BK) // BK
+    mblk, nblk = pad(M, BM) // BM, pad(N, bn) // bn
     src = (GEMM_TEMPLATE.replace("NAME", name).replace("PARAMS", params).replace("TILE_N", str(bn))
-           .replace("NSTAGES", str(stages)).replace("KBLOCKS", str(kb)).replace("TMEM_COLS", str(max(32, bn)))
+           .replace("NSTAGES", str(stages)).replace("KBLOCKS", str(kb))
+           .replace("M_BLOCKS", str(mblk)).replace("N_BLOCKS", str(nblk))
            .replace("IDX", it).replace("M_DIM", str(M)).replace("N_DIM", str(N)).replace("EPILOGUE", epi))
     stage_bytes = 2 * 128 * 128 + 2 * bn * 128
-    smem = stages * stage_bytes + 1024 + 256
-    grid = (pad(N, bn) // bn, pad(M, BM) // BM, 1)
+    smem = stages * stage_bytes + 8 * 4096 + 1024 + 256
+    grid = (min(mblk * nblk, sm_count), 1, 1)
     rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
     epi_bytes = codegen.written_reads_bytes(_epi_only(c), rngw, {})
-    return KernelSpec(name, src, bufs, grid, (128, 1, 1), smem, "gemm_tcgen05",
+    return KernelSpec(name, src, bufs, grid, (320, 1, 1), smem, "gemm_tcgen05",
                       4 * (M * K + K * N) + epi_bytes, 2 * M * N * K)
 
 
@@ -349,7 +415,7 @@ def plan(dev, cmd, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
     sb = gen_split(B, name + "_splitB", N, K, Np, Kp, "Y", "X")
     sa.extra["suffix"] = [ctypes.c_uint64(a_hi), ctypes.c_uint64(a_lo)]
     sb.extra["suffix"] = [ctypes.c_uint64(b_hi), ctypes.c_uint64(b_lo)]
-    g = gen_gemm(cmd, name + "_tc", M, N, K, bn, stages)
+    g = gen_gemm(cmd, name + "_tc", M, N, K, bn, stages, dev.ctx.sm_count)
     maps = [rt.tmap_2d(a_hi, Mp, Kp, 4 * Kp, 128, 32), rt.tmap_2d(a_lo, Mp, Kp, 4 * Kp, 128, 32),
             rt.tmap_2d(b_hi, Np, Kp, 4 * Kp, bn, 32), rt.tmap_2d(b_lo, Np, Kp, 4 * Kp, bn, 32)]
     g.extra["prefix"] = [ctypes.create_string_buffer(m, 128) for m in maps]
