@@ -31,10 +31,19 @@ from typing import Dict, List
 from . import codegen, exprs, ir
 from .codegen import Emitter, KernelSpec, cmd_buffers, dot_epilogue, dot_shape, index_type
 
+import os
+
 BM = 128
-BK = 32                 # fp32 elements of K per stage row = 128 bytes (SWIZZLE_128B)
+BK = 32                 # K padding of the split operands (multiple of every stage depth)
 BN_DEFAULT = 256
-STAGES_FOR_BN = {256: 2, 128: 3, 64: 4}
+# fp32 of K per stage row: 16 (64-byte rows, SWIZZLE_64B) or 32 (128-byte rows, SWIZZLE_128B)
+BKF = int(os.environ.get("AD_GEMM_BK", "16"))
+GROUP_M = int(os.environ.get("AD_GEMM_GROUP", "16"))
+SMEM_STAGES_BYTES = 192 * 1024
+
+
+def stages_for(bn: int, bkf: int = BKF) -> int:
+    return max(2, SMEM_STAGES_BYTES // (2 * (128 + bn) * bkf * 4))
 
 
 def pad(x: int, m: int) -> int:
@@ -161,9 +170,10 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const TmapT* map, unsigne
                  :: "r"(smem_u32(dst)), "l"((unsigned long long)map), "r"(smem_u32(bar)), "r"(c0), "r"(c1) : "memory");
 }
 __device__ __forceinline__ unsigned long long sdesc(const void* p) {
-    // K-major SWIZZLE_128B: start>>4, LBO=16B (unused), SBO=1024B, version 1, layout 2 (128B swizzle)
+    // K-major, rows of ROWB bytes swizzled in 8-row atoms: start>>4, LBO=16B (unused),
+    // SBO = 8 * ROWB, version 1, layout SWZ (2 = 128B swizzle, 4 = 64B swizzle)
     const unsigned long long a = (smem_u32(p) >> 4) & 0x3FFFull;
-    return a | (1ull << 16) | ((1024ull >> 4) << 32) | (1ull << 46) | (2ull << 61);
+    return a | (1ull << 16) | ((8ull * ROWB >> 4) << 32) | (1ull << 46) | ((unsigned long long)SWZ << 61);
 }
 __device__ __forceinline__ void mma_tf32(unsigned tmem, unsigned long long ad, unsigned long long bd, unsigned idesc, unsigned acc) {
     asm volatile("{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
@@ -175,7 +185,7 @@ __device__ __forceinline__ void mma_commit(unsigned long long* bar) {
 }
 __device__ __forceinline__ void tile_of(int t, int& m_blk, int& n_blk) {
     // grouped raster: GROUP m-blocks share each sweep over n so A panels stay in L2
-    constexpr int GROUP = 8, NUM_M = M_BLOCKS, NUM_N = N_BLOCKS;
+    constexpr int GROUP = GROUP_M, NUM_M = M_BLOCKS, NUM_N = N_BLOCKS;
     const int per_group = GROUP * NUM_N;
     const int g = t / per_group, first = g * GROUP;
     const int gsz = (NUM_M - first) < GROUP ? (NUM_M - first) : GROUP;
@@ -194,7 +204,7 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
     PARAMS int* __restrict__ err)
 {
     constexpr int BN = TILE_N, STAGES = NSTAGES, KB = KBLOCKS, NUM_TILES = M_BLOCKS * N_BLOCKS;
-    constexpr unsigned A_BYTES = 128 * 128, B_BYTES = BN * 128;
+    constexpr unsigned A_BYTES = 128 * ROWB, B_BYTES = BN * ROWB;
     constexpr unsigned STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     constexpr int EPI_WARPS = 8;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -244,10 +254,10 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
                     }
                     unsigned char* st = smem + s * STAGE_BYTES;
                     mbar_expect_tx(&full[s], STAGE_BYTES);
-                    tma_load_2d(st, &tAh, &full[s], kb * 32, mb * 128);
-                    tma_load_2d(st + A_BYTES, &tAl, &full[s], kb * 32, mb * 128);
-                    tma_load_2d(st + 2 * A_BYTES, &tBh, &full[s], kb * 32, nb * BN);
-                    tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tBl, &full[s], kb * 32, nb * BN);
+                    tma_load_2d(st, &tAh, &full[s], kb * BKF, mb * 128);
+                    tma_load_2d(st + A_BYTES, &tAl, &full[s], kb * BKF, mb * 128);
+                    tma_load_2d(st + 2 * A_BYTES, &tBh, &full[s], kb * BKF, nb * BN);
+                    tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tBl, &full[s], kb * BKF, nb * BN);
                 }
             }
             if (*abort_flag) {
@@ -286,7 +296,7 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
                     const unsigned long long ah = sdesc(st), al = sdesc(st + A_BYTES);
                     const unsigned long long bh = sdesc(st + 2 * A_BYTES), bl = sdesc(st + 2 * A_BYTES + B_BYTES);
                     #pragma unroll
-                    for (int k8 = 0; k8 < 4; ++k8) {
+                    for (int k8 = 0; k8 < BKF / 8; ++k8) {
                         const unsigned long long adv = (unsigned long long)(k8 * 32) >> 4;  // 8 fp32 = 32 bytes
                         const unsigned first = (kb > 0 || k8 > 0) ? 1u : 0u;
                         mma_tf32(d, ah + adv, bh + adv, IDESC, first);
@@ -371,13 +381,14 @@ def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int, sm_coun
     epi = dot_epilogue(c, em, it, "accv", {"X": "om", "Y": "on", "G": f"(om * ({it}){N} + on)"})
     epi = "\n                    ".join(epi.split("\n"))
     params = "".join(f"float* __restrict__ p{i}, " for i in range(len(bufs)))
-    kb = pad(K, BK) // BK
+    kb = pad(K, BK) // BKF
     mblk, nblk = pad(M, BM) // BM, pad(N, bn) // bn
     src = (GEMM_TEMPLATE.replace("NAME", name).replace("PARAMS", params).replace("TILE_N", str(bn))
-           .replace("NSTAGES", str(stages)).replace("KBLOCKS", str(kb))
+           .replace("NSTAGES", str(stages)).replace("KBLOCKS", str(kb)).replace("GROUP_M", str(GROUP_M))
+           .replace("ROWB", str(BKF * 4)).replace("SWZ", "2" if BKF == 32 else "4").replace("BKF", str(BKF))
            .replace("M_BLOCKS", str(mblk)).replace("N_BLOCKS", str(nblk))
            .replace("IDX", it).replace("M_DIM", str(M)).replace("N_DIM", str(N)).replace("EPILOGUE", epi))
-    stage_bytes = 2 * 128 * 128 + 2 * bn * 128
+    stage_bytes = 2 * 128 * BKF * 4 + 2 * bn * BKF * 4
     smem = stages * stage_bytes + 8 * 4096 + 1024 + 256
     grid = (min(mblk * nblk, sm_count), 1, 1)
     rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
@@ -406,7 +417,7 @@ def plan(dev, cmd, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
     dn, M, N, K = dot_shape(cmd)
     A, B = dn.kargs
     bn = tile_n(N)
-    stages = STAGES_FOR_BN[bn]
+    stages = stages_for(bn)
     Mp, Np, Kp = pad(M, BM), pad(N, bn), pad(K, BK)
     base = dev.scratch_base
     a_hi, a_lo = base, base + 4 * Mp * Kp
@@ -416,8 +427,9 @@ def plan(dev, cmd, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
     sa.extra["suffix"] = [ctypes.c_uint64(a_hi), ctypes.c_uint64(a_lo)]
     sb.extra["suffix"] = [ctypes.c_uint64(b_hi), ctypes.c_uint64(b_lo)]
     g = gen_gemm(cmd, name + "_tc", M, N, K, bn, stages, dev.ctx.sm_count)
-    maps = [rt.tmap_2d(a_hi, Mp, Kp, 4 * Kp, 128, 32), rt.tmap_2d(a_lo, Mp, Kp, 4 * Kp, 128, 32),
-            rt.tmap_2d(b_hi, Np, Kp, 4 * Kp, bn, 32), rt.tmap_2d(b_lo, Np, Kp, 4 * Kp, bn, 32)]
+    sw = BKF * 4
+    maps = [rt.tmap_2d(a_hi, Mp, Kp, 4 * Kp, 128, BKF, 4, sw), rt.tmap_2d(a_lo, Mp, Kp, 4 * Kp, 128, BKF, 4, sw),
+            rt.tmap_2d(b_hi, Np, Kp, 4 * Kp, bn, BKF, 4, sw), rt.tmap_2d(b_lo, Np, Kp, 4 * Kp, bn, BKF, 4, sw)]
     g.extra["prefix"] = [ctypes.create_string_buffer(m, 128) for m in maps]
     g.extra["suffix"] = [ctypes.c_uint64(dev.err_ptr)]
     g.flops = 2 * M * N * K
