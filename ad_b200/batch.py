@@ -1,0 +1,154 @@
+"""Horizontal batching: independent commands with the same kernel -> one launch.
+
+The reference's DotProd is 2-D only (autodiff/graph/compute/dotprod.py:10-16),
+so a batched transformer is traced per (sequence, head): a 4-layer, batch-32,
+8-head encoder step holds thousands of tiny dot products, softmaxes and
+elementwise commands that differ only in which buffers (or which slice of a
+buffer) they touch.  Launched one by one each would occupy a handful of SMs
+for a few microseconds.
+
+This pass re-schedules a command list by dependency level (as-soon-as-possible
+levels of the read/write dependency graph on buffer ids: read-after-write,
+write-after-read, write-after-write; host commands -- Feeder, Receiver -- keep
+their original relative order; a nested ``ForNode`` is a barrier) and groups
+the commands of one level whose generated kernel source is identical into a
+``Batched`` command.  A batched kernel receives a device table of pointer
+parameters and ``blockIdx.z`` selects the instance; its body is the unchanged
+per-command kernel.  Slice offsets of read-only buffers are already folded
+into those pointers (``codegen.view_of``), so per-sequence slices share a
+source.
+"""
+from __future__ import annotations
+
+import re
+from dataclasses import dataclass
+from typing import Callable, Dict, List, Optional, Set, Tuple
+
+from . import ir
+
+HOST = ("Feeder", "Receiver")
+
+
+@dataclass
+class Batched:
+    cmds: List
+    program_id: int = -1
+
+    def accesses(self) -> Tuple[List[int], List[int]]:
+        from .memplan import _accesses
+        r, w = [], []
+        for c in self.cmds:
+            a, b = _accesses(c)
+            r += a
+            w += b
+        return sorted(set(r)), sorted(set(w))
+
+
+def _rw(c) -> Tuple[Set[int], Set[int]]:
+    from .memplan import _accesses
+    r, w = _accesses(c)
+    return set(r), set(w)
+
+
+def schedule(body: List, signature: Callable[[object], Optional[str]]) -> List:
+    """Reorder + group ``body`` (a list of commands without Alloc/Dealloc)."""
+    out: List = []
+    seg: List = []
+    for c in body:
+        if isinstance(c, ir.ForNode):
+            out += _schedule_segment(seg, signature)
+            seg = []
+            out.append(c)
+        else:
+            seg.append(c)
+    out += _schedule_segment(seg, signature)
+    return out
+
+
+def _schedule_segment(cmds: List, signature) -> List:
+    if len(cmds) < 2:
+        return list(cmds)
+    level: List[int] = []
+    last_write: Dict[int, int] = {}        # buffer -> level of its last writer
+    last_read: Dict[int, int] = {}         # buffer -> max level of its readers since that write
+    last_host = -1
+    for c in cmds:
+        r, w = _rw(c)
+        lv = 0
+        for b in r:
+            if b in last_write:
+                lv = max(lv, last_write[b] + 1)
+        for b in w:
+            if b in last_write:
+                lv = max(lv, last_write[b] + 1)
+            if b in last_read:
+                lv = max(lv, last_read[b] + 1)
+        if type(c).__name__ in HOST:
+            lv = max(lv, last_host + 1)
+            last_host = lv
+        level.append(lv)
+        for b in r:
+            last_read[b] = max(last_read.get(b, -1), lv)
+        for b in w:
+            last_write[b] = lv
+            last_read.pop(b, None)
+    out: List = []
+    for lv in range(max(level) + 1):
+        groups: Dict[str, List] = {}
+        order: List = []
+        for c, l in zip(cmds, level):
+            if l != lv:
+                continue
+            sig = signature(c)
+            if sig is None:
+                order.append(c)
+                continue
+            if sig not in groups:
+                groups[sig] = []
+                order.append(("group", sig))
+            groups[sig].append(c)
+        for item in order:
+            if isinstance(item, tuple):
+                g = groups[item[1]]
+                out.append(g[0] if len(g) == 1 else Batched(g))
+            else:
+                out.append(item)
+    return out
+
+
+def batch_proc(proc: ir.Proc, signature) -> ir.Proc:
+    def rewrite(p: ir.Proc):
+        body = [c for c in p.procedure if type(c).__name__ not in ("AllocEntry", "DeallocEntry")]
+        for c in body:
+            if isinstance(c, ir.ForNode):
+                rewrite(c.proc)
+        head = [c for c in p.procedure if type(c).__name__ == "AllocEntry"]
+        tail = [c for c in p.procedure if type(c).__name__ == "DeallocEntry"]
+        p.procedure = head + schedule(body, signature) + tail
+
+    rewrite(proc)
+    return proc
+
+
+_SIG = re.compile(r'extern "C" __global__ void (__launch_bounds__\([^)]*\) )?(\w+)\(([^)]*)\)\s*\{')
+
+
+def batched_source(src: str, name: str) -> Tuple[str, int]:
+    """Turn ``extern "C" __global__ void K(T0* p0, ..., Tn* pn) { body }`` into a
+    kernel that reads its n pointer parameters from ``ad_tab[blockIdx.z * n + i]``."""
+    m = _SIG.search(src)
+    if m is None:
+        raise ValueError("kernel signature not found")
+    params = [x.strip() for x in m.group(3).split(",") if x.strip()]
+    decls = []
+    for i, prm in enumerate(params):
+        typ, pname = prm.rsplit(" ", 1)
+        if "*" not in typ:
+            raise ValueError(f"non-pointer parameter {prm}")
+        base = typ.replace("__restrict__", "").strip()
+        decls.append(f"    {typ} {pname} = reinterpret_cast<{base}>("
+                     f"ad_tab[(unsigned long long)blockIdx.z * {len(params)} + {i}]);")
+    lb = m.group(1) or ""
+    head = (f'extern "C" __global__ void {lb}{name}(const unsigned long long* __restrict__ ad_tab) {{\n'
+            + "\n".join(decls) + "\n")
+    return src[:m.start()] + head + src[m.end():], len(params)

@@ -87,11 +87,76 @@ class KernelSpec:
     extra: Dict = field(default_factory=dict)
 
 
-class Emitter:
-    """Lowers kargs/expressions to C++ over positional buffer params."""
+def distribute(e: ir.Expr) -> ir.Expr:
+    """Move constant terms out of ``(a + c) * m`` and ``(a + c) << s``:
+    ``a*m + c*m`` / ``(a << s) + (c << s)``.  Same integer value."""
+    if not isinstance(e, ir.Bin):
+        return e
+    if e.op == "Add":
+        return ir.Bin("Add", distribute(e.a), distribute(e.b))
+    if e.op in ("Mult", "ShiftLeft") and isinstance(e.b, ir.Const) and e.b.val >= 0:
+        inner = distribute(e.a)
+        terms = _sum_terms(inner)
+        if len(terms) == 1:
+            return ir.Bin(e.op, inner, e.b)
+        scale = e.b.val if e.op == "Mult" else (1 << e.b.val)
+        out = None
+        for t in terms:
+            u = ir.Const(t.val * scale) if isinstance(t, ir.Const) else ir.Bin(e.op, t, e.b)
+            out = u if out is None else ir.Bin("Add", out, u)
+        return out
+    return e
 
-    def __init__(self, buf_ids: Sequence[int], idx_t: str):
-        self.pos = {b: i for i, b in enumerate(buf_ids)}
+
+def _sum_terms(x: ir.Expr) -> List[ir.Expr]:
+    if isinstance(x, ir.Bin) and x.op == "Add":
+        return _sum_terms(x.a) + _sum_terms(x.b)
+    return [x]
+
+
+def split_offset(e: ir.Expr) -> Tuple[ir.Expr, int]:
+    """``e`` as ``(rest, C)`` with ``e == rest + C``: C collects the constant terms
+    of the sum after ``distribute`` (the folded Index/slice start)."""
+    terms = _sum_terms(distribute(e))
+    c = sum(t.val for t in terms if isinstance(t, ir.Const))
+    rest = [t for t in terms if not isinstance(t, ir.Const)]
+    if not rest:
+        return ir.Const(0), c
+    r = rest[0]
+    for t in rest[1:]:
+        r = ir.Bin("Add", r, t)
+    return r, c
+
+
+def _kmats_of(k) -> List[ir.KMatrix]:
+    if isinstance(k, ir.KMatrix) and not k.is_temp:
+        return [k]
+    if isinstance(k, ir.KConcat):
+        return _kmats_of(k.karg_one) + _kmats_of(k.karg_two)
+    return []
+
+
+def view_of(k: ir.KMatrix, written: set) -> Tuple[int, int]:
+    """Pointer view (buffer id, element offset) for an access.  The constant
+    offset of a read-only buffer moves into the pointer when that keeps 16-byte
+    alignment, so commands that differ only in which slice they read share one
+    kernel source (and can be batched, see ``batch.py``)."""
+    if k.id in written:
+        return (k.id, 0)
+    _, c = split_offset(k.access)
+    if c > 0 and c % 4 == 0:
+        return (k.id, c)
+    return (k.id, 0)
+
+
+class Emitter:
+    """Lowers kargs/expressions to C++ over positional pointer params.  Params
+    are *views* ``(buffer id, element offset)``: see ``view_of``."""
+
+    def __init__(self, views: Sequence, idx_t: str, written: Optional[set] = None):
+        views = [v if isinstance(v, tuple) else (v, 0) for v in views]
+        self.pos = {v: i for i, v in enumerate(views)}
+        self.written = set(written or ())
         self.idx_t = idx_t
         self.n = 0
 
@@ -99,8 +164,19 @@ class Emitter:
         self.n += 1
         return f"{prefix}{self.n}"
 
-    def p(self, buf_id: int) -> str:
-        return f"p{self.pos[buf_id]}"
+    def p(self, buf_id: int, off: int = 0) -> str:
+        return f"p{self.pos[(buf_id, off)]}"
+
+    def ref(self, k: ir.KMatrix) -> Tuple[str, ir.Expr]:
+        """(param name, index expression relative to that param) for an access."""
+        v = view_of(k, self.written)
+        if v[1]:
+            return f"p{self.pos[v]}", split_offset(k.access)[0]
+        return f"p{self.pos[v]}", k.access
+
+    def at(self, k: ir.KMatrix, env: Dict[str, str]) -> str:
+        pn, e = self.ref(k)
+        return f"{pn}[{self.expr(e, env)}]"
 
     def expr(self, e: ir.Expr, env: Dict[str, str]) -> str:
         if isinstance(e, ir.Const):
@@ -126,10 +202,36 @@ class Emitter:
         if isinstance(k, ir.KMatrix):
             if k.is_temp:
                 return temps[k.id]
-            return f"{self.p(k.id)}[{self.expr(k.access, env)}]"
+            return self.at(k, env)
         c = self.expr(k.condition, env)
         return (f"({c} ? ({self.scalar_karg(k.karg_two, env, temps)}) : "
                 f"({self.scalar_karg(k.karg_one, env, temps)}))")
+
+
+def cmd_written(c) -> set:
+    w = set()
+    for n in chain_nodes(c):
+        w |= set(n.kres.ids(True))
+    return w
+
+
+def cmd_views(c, written: Optional[set] = None) -> List[Tuple[int, int]]:
+    """Sorted pointer views of a command (see ``view_of``)."""
+    written = cmd_written(c) if written is None else written
+    vs = set()
+    for n in chain_nodes(c):
+        for k in n.kargs:
+            for km in _kmats_of(k):
+                vs.add(view_of(km, written))
+        for km in _kmats_of(n.kres):
+            vs.add(view_of(km, written))
+    return sorted(vs)
+
+
+def make_emitter(c, idx_t: str):
+    w = cmd_written(c)
+    views = cmd_views(c, w)
+    return views, Emitter(views, idx_t, w)
 
 
 def karg_buffers(k: ir.KernelArg) -> List[int]:
@@ -219,10 +321,9 @@ def gen_elementwise(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
     item per element of ``prod(shape)`` with ``_global_id`` = element index."""
     kind = type(c).__name__
     n_el = math.prod(c.init_node.shape if kind == "ElwFuse" else c.shape)
-    bufs = cmd_buffers(c)
     rng = {"G": (0, max(n_el - 1, 0))}
     it = index_type(c, rng)
-    em = Emitter(bufs, it)
+    bufs, em = make_emitter(c, it)
     nodes = chain_nodes(c)
 
     def body_vec() -> List[str]:
@@ -243,21 +344,20 @@ def gen_elementwise(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
                         lines.append(f"const float {out_vars[j]} = {temps_l[j][k.id]};")
                     return
                 ln = exprs.lanes(k.access, "G", VEC)
-                p = em.p(k.id)
                 if ln.unit(VEC):
                     v = em.tmp("q")
-                    lines.append(f"const float4 {v} = *reinterpret_cast<const float4*>(&{p}[{em.expr(k.access, env0)}]);")
+                    lines.append(f"const float4 {v} = *reinterpret_cast<const float4*>(&{em.at(k, env0)});")
                     for j, comp in enumerate("xyzw"):
                         lines.append(f"const float {out_vars[j]} = {v}.{comp};")
                 elif ln.uniform:
                     v = em.tmp("u")
-                    lines.append(f"const float {v} = {p}[{em.expr(k.access, env0)}];")
+                    lines.append(f"const float {v} = {em.at(k, env0)};")
                     for j in range(VEC):
                         lines.append(f"const float {out_vars[j]} = {v};")
                 else:
                     for j in range(VEC):
                         env = {"G": f"(g0 + ({it}){j})"}
-                        lines.append(f"const float {out_vars[j]} = {p}[{em.expr(k.access, env)}];")
+                        lines.append(f"const float {out_vars[j]} = {em.at(k, env)};")
                 return
             # KConcat: cond ? two : one (opencl/karg.py:52)
             lc = exprs.lanes(k.condition, "G", VEC)
@@ -305,14 +405,13 @@ def gen_elementwise(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
                     temps_l[j][kres.id] = t
                 continue
             ln = exprs.lanes(kres.access, "G", VEC)
-            p = em.p(kres.id)
             if ln.unit(VEC):
-                lines.append(f"*reinterpret_cast<float4*>(&{p}[{em.expr(kres.access, env0)}]) = "
+                lines.append(f"*reinterpret_cast<float4*>(&{em.at(kres, env0)}) = "
                              f"make_float4({', '.join(res)});")
             else:
                 for j in range(VEC):
                     env = {"G": f"(g0 + ({it}){j})"}
-                    lines.append(f"{p}[{em.expr(kres.access, env)}] = {res[j]};")
+                    lines.append(f"{em.at(kres, env)} = {res[j]};")
         return lines
 
     def body_scalar() -> List[str]:
@@ -333,7 +432,7 @@ def gen_elementwise(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
                 lines.append(f"const float {t} = {r};")
                 temps[nd.kres.id] = t
             else:
-                lines.append(f"{em.p(nd.kres.id)}[{em.expr(nd.kres.access, env)}] = {r};")
+                lines.append(f"{em.at(nd.kres, env)} = {r};")
         return lines
 
     vec_ok = n_el >= VEC
@@ -384,10 +483,9 @@ def gen_reduce(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
     V, R = rn.children_shapes[0]
     op = rn.op
     src_k = rn.kargs[0]
-    bufs = cmd_buffers(c)
     rng = {"X": (0, V - 1), "Y": (0, max(R - 1, 0)), "G": (0, V - 1)}
     it = index_type(c, rng)
-    em = Emitter(bufs, it)
+    bufs, em = make_emitter(c, it)
     ident = "0.0f" if op == "SUM" else "(__int_as_float(0xff800000))"
     comb = (lambda a, b: f"({a} + {b})") if op == "SUM" else (lambda a, b: f"fmaxf({a}, {b})")
 
@@ -408,7 +506,7 @@ def gen_reduce(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
                 lines.append(f"const float {t} = {r};")
                 temps[nd.kres.id] = t
             else:
-                lines.append(f"{em.p(nd.kres.id)}[{em.expr(nd.kres.access, env)}] = {r};")
+                lines.append(f"{em.at(nd.kres, env)} = {r};")
         return "\n            ".join(lines)
 
     params = ", ".join(f"float* __restrict__ p{i}" for i in range(len(bufs)))
@@ -461,7 +559,7 @@ def gen_reduce(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
         upt = min(upt_all, 8)          # loads per thread in flight before combining
         chunks = (upt_all + upt - 1) // upt
         if row_vec:
-            ldv = (f"*reinterpret_cast<const float4*>(&{em.p(src_k.id)}[{em.expr(src_k.access, env)}])")
+            ldv = (f"*reinterpret_cast<const float4*>(&{em.at(src_k, env)})")
             load_stmt = f"if (yy < ({it}){R}) q[u] = {ldv};"
             fold = f"acc = {comb(comb('acc', 'q[u].x'), comb('q[u].y', comb('q[u].z', 'q[u].w')))};"
             qdecl = f"float4 q[{upt}];"
@@ -523,8 +621,7 @@ def gen_reduce(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
     ny = 32 if R >= 256 else 8
     env = {"X": "xq", "Y": "yy", "G": "xq"}
     if col_vec:
-        ld = (f"{{ const float4 q = *reinterpret_cast<const float4*>(&{em.p(src_k.id)}"
-              f"[{em.expr(src_k.access, env)}]);\n"
+        ld = (f"{{ const float4 q = *reinterpret_cast<const float4*>(&{em.at(src_k, env)});\n"
               f"            a0 = {comb('a0', 'q.x')}; a1 = {comb('a1', 'q.y')}; a2 = {comb('a2', 'q.z')}; a3 = {comb('a3', 'q.w')}; }}")
         accs = ["a0", "a1", "a2", "a3"]
     else:
@@ -577,7 +674,7 @@ def dot_epilogue(c, em: Emitter, it: str, acc: str, env: Dict[str, str]) -> str:
             lines.append(f"const float {t} = {r};")
             temps[nd.kres.id] = t
         else:
-            lines.append(f"{em.p(nd.kres.id)}[{em.expr(nd.kres.access, env)}] = {r};")
+            lines.append(f"{em.at(nd.kres, env)} = {r};")
     return "\n".join(lines)
 
 
@@ -593,10 +690,9 @@ def gen_dot_simt(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
     in shared memory through the operands' access expressions (any
     Permute/Concat/constant), fp32 FMA accumulation, fused epilogue."""
     dn, M, N, K = dot_shape(c)
-    bufs = cmd_buffers(c)
     rng = {"X": (0, max(M, K) - 1), "Y": (0, max(N, K) - 1), "G": (0, M * N - 1)}
     it = index_type(c, rng)
-    em = Emitter(bufs, it)
+    bufs, em = make_emitter(c, it)
     A, B = dn.kargs
     la = em.scalar_karg(A, {"X": "gm", "Y": "gk"}, {})
     lb = em.scalar_karg(B, {"X": "gk", "Y": "gn"}, {})
@@ -661,10 +757,9 @@ def gen_dot_warp(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
     examples/linear.py): one warp per output element, lanes stride over K,
     shuffle reduction, lane 0 runs the fused epilogue."""
     dn, M, N, K = dot_shape(c)
-    bufs = cmd_buffers(c)
     rng = {"X": (0, max(M, K) - 1), "Y": (0, max(N, K) - 1), "G": (0, M * N - 1)}
     it = index_type(c, rng)
-    em = Emitter(bufs, it)
+    bufs, em = make_emitter(c, it)
     A, B = dn.kargs
     la = em.scalar_karg(A, {"X": "om", "Y": "kk"}, {})
     lb = em.scalar_karg(B, {"X": "kk", "Y": "on"}, {})

@@ -63,9 +63,11 @@ class CudaB200Device:
     """Device plug-in with the reference's interface (device/__init__.py:1-6)."""
 
     def __init__(self, device: int = 0, use_graphs: bool = True, gemm: str = "auto",
-                 verbose: bool = False, comm=None, rowfuse: bool = True):
+                 verbose: bool = False, comm=None, rowfuse: bool = True, batch: bool = True):
         self.ctx = rt.Context(device)
         self.rowfuse = rowfuse and os.environ.get("AD_ROWFUSE", "1") != "0"
+        self.batch = batch and os.environ.get("AD_BATCH", "1") != "0"
+        self._spec_cache: Dict[int, codegen.KernelSpec] = {}
         self.use_graphs = use_graphs and os.environ.get("AD_GRAPH", "1") != "0"
         self.gemm = os.environ.get("AD_GEMM", gemm)
         self.verbose = verbose
@@ -111,23 +113,67 @@ class CudaB200Device:
         return out
 
     # ------------------------------------------------------------ init pass
+    def _single_spec(self, cmd, sizes) -> Optional[codegen.KernelSpec]:
+        """The one pointer-only kernel of ``cmd``, or None when it needs several
+        launches or non-pointer arguments (the tensor-core dot path)."""
+        key = id(cmd)
+        if key in self._spec_cache:
+            return self._spec_cache[key]
+        kind = type(cmd).__name__
+        name = f"k_{kind}"
+        spec = None
+        if kind in ELEMENTWISE:
+            spec = codegen.gen_elementwise(cmd, name, sizes)
+        elif kind in REDUCE:
+            spec = codegen.gen_reduce(cmd, name, sizes)
+        elif kind in DOT:
+            from . import gemm
+            spec = gemm.single_kernel_spec(self, cmd, name, sizes)
+        elif kind == "RowFused":
+            from . import rowfuse
+            spec = rowfuse.gen_rowfused(cmd, "k_RowFused", sizes, self.ctx.sm_count)
+            spec.extra["err_param"] = True
+        self._spec_cache[key] = spec
+        return spec
+
     def _specs_for(self, cmd) -> List[codegen.KernelSpec]:
         kind = type(cmd).__name__
         sizes = {b: s.size for b, s in self.slots.items()}
         name = f"k_{kind}"
-        if kind in ELEMENTWISE:
-            return [codegen.gen_elementwise(cmd, name, sizes)]
-        if kind in REDUCE:
-            return [codegen.gen_reduce(cmd, name, sizes)]
+        if kind == "Batched":
+            from . import batch
+            members = [self._single_spec(c, sizes) for c in cmd.cmds]
+            first = members[0]
+            src, nparam = batch.batched_source(first.src, first.name + "_x")
+            spec = codegen.KernelSpec(first.name + "_x", src, [], (first.grid[0], first.grid[1], len(members)),
+                                      first.block, first.smem, first.kind + "_batched",
+                                      sum(m.bytes_moved for m in members), sum(m.flops for m in members))
+            spec.extra["table"] = [(m.buffers, bool(m.extra.get("err_param"))) for m in members]
+            spec.extra["nparam"] = nparam
+            return [spec]
+        single = self._single_spec(cmd, sizes)
+        if single is not None:
+            if single.extra.get("err_param"):
+                single.extra["suffix"] = [ctypes.c_uint64(self.err_ptr)]
+            return [single]
         if kind in DOT:
             from . import gemm
             return gemm.plan_dot(self, cmd, name, sizes)
-        if kind == "RowFused":
-            from . import rowfuse
-            spec = rowfuse.gen_rowfused(cmd, "k_RowFused", sizes, self.ctx.sm_count)
-            spec.extra["suffix"] = [ctypes.c_uint64(self.err_ptr)]
-            return [spec]
         raise TypeError(f"Encountered unexpected cmd: {kind}")
+
+    def _upload_table(self, spec) -> int:
+        """Device table of pointer parameters of a batched launch (instance-major)."""
+        rows = []
+        for bufs, err in spec.extra["table"]:
+            row = [self.view_ptr(v) for v in bufs] + ([self.err_ptr] if err else [])
+            assert len(row) == spec.extra["nparam"]
+            rows += row
+        a = np.asarray(rows, dtype=np.uint64)
+        p = self.ctx.malloc(a.nbytes)
+        self.scratch_allocs.append(p)
+        self.ctx.h2d(p, a.ctypes.data, a.nbytes, 0)
+        self.ctx.sync(0)
+        return p
 
     def init(self, cmd) -> None:
         """Per-command init (opencl/device.py:46-86): kernels are generated here
@@ -164,13 +210,20 @@ class CudaB200Device:
         for cmd, specs in self._pending:
             ls = []
             for s in specs:
-                ptrs = [self.ptr(b) if b >= 0 else self.scratch_ptr(b) for b in s.buffers]
+                if "table" in s.extra:
+                    ls.append(Launch(s, self.kernels[s.src], [self._upload_table(s)], {}))
+                    continue
+                ptrs = [self.view_ptr(v) for v in s.buffers]
                 ls.append(Launch(s, self.kernels[s.src], ptrs, s.extra))
             self.launches[id(cmd)] = ls
         self._pending = []
 
-    def scratch_ptr(self, b: int) -> int:
-        return self.scratch[b]
+    def view_ptr(self, v) -> int:
+        """Device address of a kernel pointer parameter: a buffer, or a
+        (buffer, element offset) view of one."""
+        if isinstance(v, tuple):
+            return self.ptr(v[0]) + 4 * v[1]
+        return self.ptr(v)
 
     # ------------------------------------------------------------ run pass
     def _launch(self, L: Launch, stream: int = 0) -> None:
@@ -307,6 +360,19 @@ class CudaB200Device:
         if self.rowfuse:
             from . import rowfuse
             rowfuse.fuse_rows(proc)
+        if self.batch:
+            from . import batch
+            sizes: Dict[int, int] = {}
+            for c in ir.iter_cmds(proc):
+                if isinstance(c, ir.AllocEntry) and not c.is_temp:
+                    sizes[c.id] = max(sizes.get(c.id, 0), c.size)
+
+            def signature(c):
+                if type(c).__name__ not in ir.COMPUTE_KINDS:
+                    return None
+                sp = self._single_spec(c, sizes)
+                return None if sp is None else sp.src
+            batch.batch_proc(proc, signature)
         self.proc = proc
         self._pinned_ptrs: List[int] = []
         self._setup_memory(proc)

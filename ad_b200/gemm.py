@@ -24,7 +24,22 @@ def use_tensor_cores(dev, M: int, N: int, K: int) -> bool:
         return False
     if mode == "tc":
         return True
-    return M * N * K >= (1 << 21) and min(M, N) >= 16 and K >= 8
+    if M * N * K < (1 << 21) or min(M, N) < 16 or K < 8:
+        return False
+    # too few output tiles to occupy the GPU: the CUDA-core kernel, which batches
+    # across independent commands (e.g. per-head projections), does better
+    from .tcgen05 import BM, pad, tile_n
+    tiles = (pad(M, BM) // BM) * (pad(N, tile_n(N)) // tile_n(N))
+    return tiles >= 64 or (tiles >= 8 and M * N * K >= (1 << 27))
+
+
+def single_kernel_spec(dev, cmd, name: str, sizes: Dict[int, int]):
+    """The CUDA-core kernel of a dot product that does not take the tensor-core
+    path (one launch, pointer parameters only), else None."""
+    dn, M, N, K = codegen.dot_shape(cmd)
+    if use_tensor_cores(dev, M, N, K):
+        return None
+    return plan_dot(dev, cmd, name, sizes)[0]
 
 
 def plan_dot(dev, cmd, name: str, sizes: Dict[int, int]) -> List[codegen.KernelSpec]:
@@ -32,7 +47,7 @@ def plan_dot(dev, cmd, name: str, sizes: Dict[int, int]) -> List[codegen.KernelS
     if use_tensor_cores(dev, M, N, K):
         from . import tcgen05
         return tcgen05.plan(dev, cmd, name, sizes)
-    if K >= 32 and M * N <= 32768:
+    if K >= 32 and M * N <= 4096:
         return [codegen.gen_dot_warp(cmd, name + "_warp", sizes)]
     return [codegen.gen_dot_simt(cmd, name + "_simt", sizes)]
 

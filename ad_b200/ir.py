@@ -317,7 +317,7 @@ class ForNode:
 
 
 COMPUTE_KINDS = ("BinaryNode", "UnaryNode", "ContigiousNode", "ReduceNode",
-                 "DotProdNode", "ElwFuse", "ReduceElwFuse", "DPElwFuse", "RowFused")
+                 "DotProdNode", "ElwFuse", "ReduceElwFuse", "DPElwFuse", "RowFused", "Batched")
 
 # --------------------------------------------------------------------------
 # Conversion from the reference's live objects (duck-typed by class name)

@@ -408,10 +408,13 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
         raise ValueError("row too long for row fusion")
     rows_pb = max(1, 256 // gs) if gs < 256 else 1
     block = gs * rows_pb
-    bufs: List[int] = []
+    written_all: Set[int] = set()
     for c in rf.cmds:
-        bufs += codegen.cmd_buffers(c)
-    bufs = sorted(set(b for b in bufs if b not in rf.internal))
+        written_all |= codegen.cmd_written(c)
+    views = set()
+    for c in rf.cmds:
+        views |= set(codegen.cmd_views(c, written_all))
+    bufs = sorted(v for v in views if v[0] not in rf.internal)
     rng = {"G": (0, V * R - 1), "X": (0, V - 1), "Y": (0, R - 1)}
     it = "int"
     for c in rf.cmds:
@@ -419,7 +422,7 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
             it = "long long"
     if V * R >= (1 << 31) - 64:
         it = "long long"
-    em = Emitter(bufs, it)
+    em = Emitter(bufs, it, written_all)
     lines: List[str] = []
     st_run = run_state(rf.cmds, V, R)
     kinds = st_run.kinds
@@ -486,19 +489,18 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
                     out.extend(f"{q}.{cmp}" for cmp in "xyzw")
                     return
                 ln = exprs.lanes(karg.access, "G", VEC)
-                p = em.p(karg.id)
                 if ln.unit(VEC):
                     q = em.tmp("q")
-                    lines.append(f"const float4 {q} = *reinterpret_cast<const float4*>(&{p}[{em.expr(karg.access, env0)}]);")
+                    lines.append(f"const float4 {q} = *reinterpret_cast<const float4*>(&{em.at(karg, env0)});")
                     out.extend(f"{q}.{cmp}" for cmp in "xyzw")
                 elif ln.uniform:
                     u = em.tmp("u")
-                    lines.append(f"const float {u} = {p}[{em.expr(karg.access, env0)}];")
+                    lines.append(f"const float {u} = {em.at(karg, env0)};")
                     out.extend([u] * VEC)
                 else:
                     for j in range(VEC):
                         u = em.tmp("u")
-                        lines.append(f"const float {u} = {p}[{em.expr(karg.access, {'G': f'(g{k} + ({it}){j})'})}];")
+                        lines.append(f"const float {u} = {em.at(karg, {'G': f'(g{k} + ({it}){j})'})};")
                         out.append(u)
                 return
             for j in range(VEC):   # KConcat on an input buffer: per-lane select
@@ -536,7 +538,7 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
                     lines.append(f"{row_regs[b][k][j]} = {tv[j]};")
                 defined.add((b, k))
                 if b not in rf.internal:
-                    lines.append(f"if (live) *reinterpret_cast<float4*>(&{em.p(b)}[{em.expr(n.kres.access, env0)}]) = "
+                    lines.append(f"if (live) *reinterpret_cast<float4*>(&{em.at(n.kres, env0)}) = "
                                  f"make_float4({', '.join(tv)});")
             else:
                 raise AssertionError("full-size write to a non-row buffer")
@@ -556,7 +558,7 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
                         args.append(sc_regs[karg.id])
                     elif isinstance(karg, ir.KMatrix) and not karg.is_temp:
                         u = em.tmp("u")
-                        lines.append(f"const float {u} = live ? {em.p(karg.id)}[{em.expr(karg.access, env)}] : 0.0f;")
+                        lines.append(f"const float {u} = live ? {em.at(karg, env)} : 0.0f;")
                         args.append(u)
                     else:
                         args.append(em.scalar_karg(karg, env, temps))
@@ -573,7 +575,7 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
             lines.append(f"{sc_regs[b]} = {tv};")
             defined.add(b)
             if b not in rf.internal:
-                lines.append(f"if (live && tig == 0) {em.p(b)}[{em.expr(n.kres.access, env)}] = {tv};")
+                lines.append(f"if (live && tig == 0) {em.at(n.kres, env)} = {tv};")
 
     # consecutive reductions are independent of each other (a reduction reads a full
     # row buffer and writes per-row scalars), so a group of them shares one
@@ -627,8 +629,8 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
                     ly = exprs.lanes(src.access, "Y", VEC) if isinstance(src, ir.KMatrix) else exprs.OTHER
                     if ly.unit(VEC):
                         q = em.tmp("q")
-                        lines.append(f"const float4 {q} = live ? *reinterpret_cast<const float4*>(&{em.p(src.id)}"
-                                     f"[{em.expr(src.access, env0)}]) : make_float4({ident}, {ident}, {ident}, {ident});")
+                        lines.append(f"const float4 {q} = live ? *reinterpret_cast<const float4*>(&{em.at(src, env0)})"
+                                     f" : make_float4({ident}, {ident}, {ident}, {ident});")
                         lines.append(f"{acc} = {comb(acc, comb(comb(q + '.x', q + '.y'), comb(q + '.z', q + '.w')))};")
                     else:
                         for j in range(VEC):
@@ -679,7 +681,7 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
         body = "\n        ".join(body_lines)
         row_bytes = R * 4
         issue = "\n            ".join(
-            f"bulk_g2s(&stg[(s * {len(staged)} + {i}) * {U}], {em.p(b)} + ({it})row * {R}, {row_bytes}u, &bar[s]);"
+            f"bulk_g2s(&stg[(s * {len(staged)} + {i}) * {U}], {em.p(b, 0)} + ({it})row * {R}, {row_bytes}u, &bar[s]);"
             for i, b in enumerate(staged))
         src = f"""
 __device__ __forceinline__ unsigned rf_smem(const void* p) {{ return (unsigned)__cvta_generic_to_shared(p); }}

@@ -66,7 +66,7 @@ def gen_split(karg: ir.KernelArg, name: str, rows: int, kdim: int, rows_p: int, 
               row_var: str, k_var: str) -> KernelSpec:
     """Gather operand(row, k) via its access expression into K-major hi/lo arrays.
     ``row_var``/``k_var`` say which of the reference's X/Y carries row and k."""
-    bufs = sorted(set(karg.ids(True)))
+    bufs = sorted({codegen.view_of(km, set()) for km in codegen._kmats_of(karg)})
     rng = {"X": (0, max(rows, kdim)), "Y": (0, max(rows, kdim)), "G": (0, 0)}
     it = "int"
     for e in _karg_exprs(karg):
@@ -374,10 +374,9 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
 
 
 def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int, sm_count: int = 148) -> KernelSpec:
-    bufs = cmd_buffers(c)
     rng = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
     it = index_type(_epi_only(c), rng)
-    em = Emitter(bufs, it)
+    bufs, em = codegen.make_emitter(c, it)
     epi = dot_epilogue(c, em, it, "accv", {"X": "om", "Y": "on", "G": f"(om * ({it}){N} + on)"})
     epi = "\n                    ".join(epi.split("\n"))
     params = "".join(f"float* __restrict__ p{i}, " for i in range(len(bufs)))

@@ -37,6 +37,14 @@ WORKLOADS = {
     "mlp": {"case": "mlp", "metric": "Linear MLP train steps/s (examples/linear.py: 255-255-255, batch 2, SGD)",
             "unit": "steps/s", "loop": True, "cpu_iters": 300,
             "data": "Feeder of np.full((2,255), 0.2); weights from np.random.seed(0) randn (reference init)"},
+    "enc": {"case": "enc_4_32_128_512_8_2048_100",
+            "metric": "encoder train steps/s (4 layers, d512, 8 heads, ff2048, S128, B32, fp32, SGD)",
+            "unit": "steps/s", "loop": True, "cpu_iters": 1,
+            "data": "synthetic: x ~ N(0,1) [4096, 512] seed 0 via Feeder; Xavier-uniform weights (seeded)"},
+    "enc_small": {"case": "enc_1_8_128_512_8_2048_100",
+                  "metric": "encoder train steps/s (1 layer, d512, 8 heads, ff2048, S128, B8, fp32, SGD)",
+                  "unit": "steps/s", "loop": True, "cpu_iters": 1,
+                  "data": "synthetic: x ~ N(0,1) [1024, 512] seed 0 via Feeder; Xavier-uniform weights (seeded)"},
     "dotsig": {"case": "dotsig_4096", "data": "synthetic: X, W, b ~ U(-1/64, 1/64), dz ~ N(0,1), seeded numpy default_rng", "metric": "fused DotProd+sigmoid fwd+bwd TFLOP/s (fp32 4096^3)",
                "unit": "TFLOP/s", "flops": 3 * 2 * 4096 ** 3, "inputs": ("X_id", "dz_id"),
                "cpu_dot_rows": 16, "dot_m": 4096},
