@@ -63,8 +63,19 @@ class CudaB200Device:
     """Device plug-in with the reference's interface (device/__init__.py:1-6)."""
 
     def __init__(self, device: int = 0, use_graphs: bool = True, gemm: str = "auto",
-                 verbose: bool = False, comm=None, rowfuse: bool = True, batch: bool = True):
+                 verbose: bool = False, comm=None, rowfuse: bool = True, batch: bool = True,
+                 dp: Optional[tuple] = None, nccl_timeout_s: float = 120.0):
+        """``dp = (rank, world, uid)``: data-parallel rank of ``world``; ``uid`` is
+        the 128-byte NCCL id from ``ad_b200.dist.nccl_unique_id()`` on rank 0,
+        shared with every rank by the caller.  The proc is then this rank's shard
+        and gradients are summed over ranks (``ad_b200.dist``)."""
         self.ctx = rt.Context(device)
+        self.world = 1
+        if dp is not None and dp[1] > 1:
+            rank, world, uid = dp
+            buf = ctypes.create_string_buffer(bytes(uid), 128)
+            rt.check(self.ctx.L.ad_nccl_init(self.ctx.h, rank, world, buf, nccl_timeout_s), "ad_nccl_init")
+            self.rank, self.world = rank, world
         self.rowfuse = rowfuse and os.environ.get("AD_ROWFUSE", "1") != "0"
         self.batch = batch and os.environ.get("AD_BATCH", "1") != "0"
         self._spec_cache: Dict[int, codegen.KernelSpec] = {}
@@ -187,7 +198,7 @@ class CudaB200Device:
                 if off < 0 or off + n > self.slots[k.id].size:
                     raise ValueError(f"{kind} access out of range for buffer {k.id}")
             return
-        if kind in ("AllocEntry", "DeallocEntry", "ForNode"):
+        if kind in ("AllocEntry", "DeallocEntry", "ForNode", "AllReduce"):
             return
         self._pending.append((cmd, self._specs_for(cmd)))
 
@@ -258,7 +269,8 @@ class CudaB200Device:
                 cmd.func(*outs)
             return
         if kind == "AllReduce":
-            cmd.run(self)
+            p = self.ptr(cmd.buf) + 4 * cmd.offset
+            rt.check(self.ctx.L.ad_allreduce_f32(self.ctx.h, p, p, cmd.count, 0, 0), "ad_allreduce_f32")
             return
         for L in self.launches[id(cmd)]:
             self._launch(L)
@@ -357,6 +369,9 @@ class CudaB200Device:
     def prepare(self, proc) -> ir.Proc:
         """Init pass: plan + allocate memory, upload contents, build all kernels."""
         proc = ir.copy_structure(ir.conv_proc(proc))
+        if self.world > 1:
+            from . import dist
+            dist.insert_grad_allreduce(proc)
         if self.rowfuse:
             from . import rowfuse
             rowfuse.fuse_rows(proc)

@@ -18,6 +18,17 @@ PROC_DIR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__
 
 
 def make_array(spec: Dict) -> np.ndarray:
+    """``spec["part_rows"]`` (optional) selects rows ``[part*part_rows, (part+1)*part_rows)``
+    of the full array: one data-parallel rank's share of a global batch."""
+    a = _make_full(spec)
+    if "part_rows" in spec:
+        r = spec["part_rows"]
+        k = spec.get("part", 0)
+        a = np.ascontiguousarray(a[k * r:(k + 1) * r])
+    return a
+
+
+def _make_full(spec: Dict) -> np.ndarray:
     rng = np.random.default_rng(spec["seed"])
     shape = tuple(spec["shape"])
     if spec["dist"] == "normal":
@@ -29,14 +40,20 @@ def make_array(spec: Dict) -> np.ndarray:
     raise ValueError(spec["dist"])
 
 
-def load_case(case: str, path: Optional[str] = None, with_content: bool = True):
-    """Returns ``(proc, meta)`` with every AllocEntry content materialised."""
+def load_case(case: str, path: Optional[str] = None, with_content: bool = True, rank: int = 0):
+    """Returns ``(proc, meta)`` with every AllocEntry content materialised.  For a
+    data-parallel fixture (``meta["dp_parts"] > 1``) ``rank`` picks that rank's rows
+    of the per-example data (inputs and the fixed loss weights)."""
     proc, meta = ir.load_proc(path or os.path.join(PROC_DIR, f"{case}.json.gz"))
+
+    def with_rank(sp):
+        return dict(sp, part=rank) if "part_rows" in sp else sp
+
     if with_content:
         specs = meta.get("content_specs", {})
         for c in ir.iter_cmds(proc):
             if isinstance(c, ir.AllocEntry) and str(c.id) in specs:
-                c.content = make_array(specs[str(c.id)]).reshape(-1)
+                c.content = make_array(with_rank(specs[str(c.id)])).reshape(-1)
     for c in ir.iter_cmds(proc):
         if isinstance(c, ir.Feeder):
             f = meta.get("feeders", {}).get(c.name)
@@ -44,7 +61,7 @@ def load_case(case: str, path: Optional[str] = None, with_content: bool = True):
                 val, shape = f["fill"], tuple(f["shape"])
                 c.func = lambda val=val, shape=shape: np.full(shape, val, dtype=np.float32)
             elif f is not None and "spec" in f:
-                arr = make_array(f["spec"])
+                arr = make_array(with_rank(f["spec"]))
                 c.func = lambda arr=arr: arr
     return proc, meta
 

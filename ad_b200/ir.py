@@ -195,6 +195,7 @@ class AllocEntry:
     size: int
     content: Optional[np.ndarray] = None
     is_temp: bool = False
+    alias: Optional[tuple] = None     # (base id, element offset): a view into another buffer
 
 
 @dataclass

@@ -74,7 +74,11 @@ def plan(proc: ir.Proc) -> Tuple[Dict[int, Slot], int]:
     """Returns ({buffer id: Slot}, arena bytes)."""
     sizes: Dict[int, int] = {}
     content: Dict[int, bool] = {}
+    alias: Dict[int, tuple] = {}
     for c in ir.iter_cmds(proc):
+        if isinstance(c, ir.AllocEntry) and not c.is_temp and getattr(c, "alias", None):
+            alias[c.id] = (c.alias[0], c.alias[1], c.size)
+            continue
         if isinstance(c, ir.AllocEntry) and not c.is_temp:
             sizes[c.id] = max(sizes.get(c.id, 0), c.size)
             content[c.id] = content.get(c.id, False) or c.content is not None
@@ -84,6 +88,8 @@ def plan(proc: ir.Proc) -> Tuple[Dict[int, Slot], int]:
     pos = [0]
 
     def touch(b: int, p: int) -> None:
+        if b in alias:           # a view: its accesses keep the base buffer alive
+            b = alias[b][0]
         first[b] = min(first.get(b, p), p)
         last[b] = max(last.get(b, p), p)
 
@@ -106,6 +112,9 @@ def plan(proc: ir.Proc) -> Tuple[Dict[int, Slot], int]:
                     for b in w:
                         body_first.setdefault(b, "w")
                 for b, kind in body_first.items():
+                    if b in alias:
+                        b = alias[b][0]
+                        kind = "r"        # partial writes through views: keep the base loop-live
                     local = kind == "w" and b not in mark_before
                     if not local:
                         touch(b, start)
@@ -134,7 +143,7 @@ def plan(proc: ir.Proc) -> Tuple[Dict[int, Slot], int]:
             s, e = first[b], last[b]
         slots[b] = Slot(b, n, s, e, pinned=content.get(b, False))
     # any buffer referenced without an AllocEntry is an error in the proc
-    for b in first:
+    for b in list(first):
         if b not in slots:
             raise ValueError(f"buffer {b} is used but never allocated")
 
@@ -153,4 +162,7 @@ def plan(proc: ir.Proc) -> Tuple[Dict[int, Slot], int]:
         sl.offset = off
         placed.append(sl)
         total = max(total, off + need)
+    for a, (base, off, n) in alias.items():
+        if base in slots:
+            slots[a] = Slot(a, n, slots[base].start, slots[base].end, slots[base].offset + 4 * off)
     return slots, total

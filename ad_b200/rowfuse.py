@@ -330,14 +330,9 @@ def _flat_positions(proc: ir.Proc):
             if k in ("AllocEntry", "DeallocEntry"):
                 continue
             pos_of[id(c)] = counter[0]
-            bufs = []
-            if k == "Feeder":
-                bufs = c.kres.ids(True)
-            elif k == "Receiver":
-                for kk in c.kargs:
-                    bufs += kk.ids(True)
-            else:
-                bufs = codegen.cmd_buffers(c)
+            from .memplan import _accesses
+            r, w = _accesses(c)
+            bufs = sorted(set(r) | set(w))
             for b in bufs:
                 uses.setdefault(b, []).append(counter[0])
             counter[0] += 1

@@ -263,8 +263,11 @@ class OracleDevice:
         self.proc = proc
         srcs = {}
         self._cmds = []
+        aliases = []
         for c in ir.iter_cmds(proc):
-            if isinstance(c, ir.AllocEntry) and not c.is_temp:
+            if isinstance(c, ir.AllocEntry) and not c.is_temp and getattr(c, "alias", None):
+                aliases.append(c)
+            elif isinstance(c, ir.AllocEntry) and not c.is_temp:
                 buf = np.zeros(c.size, dtype=np.float32)
                 if c.content is not None:
                     buf[:] = np.asarray(c.content, dtype=np.float32).reshape(-1)
@@ -273,6 +276,9 @@ class OracleDevice:
                 name = f"k{len(srcs)}"
                 srcs[name] = gen_kernel(c, name, self.faithful_tree, self.dot_rows)
                 self._cmds.append((c, name))
+        for c in aliases:   # views into another buffer (ad_b200.dist gradient slices)
+            base, off = c.alias
+            self.buffers[c.id] = self.buffers[base][off:off + c.size]
         lib = compile_kernels(srcs) if srcs else None
         for c, name in self._cmds:
             fn = getattr(lib, name)
@@ -292,6 +298,9 @@ class OracleDevice:
             assert isinstance(arr, np.ndarray) and list(arr.shape) == list(c.shape), "Invalid function"
             off = offset_of(c.kres)
             self.buffers[c.kres.id][off:off + arr.size] = arr.reshape(-1)
+        elif kind == "AllReduce":
+            # data-parallel gradient sum (ad_b200.dist): the test supplies c.comm
+            c.comm(self.buffers[c.buf][c.offset:c.offset + c.count])
         elif kind == "Receiver":
             outs = []
             for k in c.kargs:
