@@ -699,9 +699,23 @@ def gen_dot_simt(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
     epi = dot_epilogue(c, em, it, "accv", {"X": "om", "Y": "on", "G": f"(om * ({it}){N} + on)"})
     epi = "\n                ".join(epi.split("\n"))
     params = ", ".join(f"float* __restrict__ p{i}" for i in range(len(bufs)))
+
+    def contiguous(k, var):
+        return isinstance(k, ir.KMatrix) and not k.is_temp and exprs.lanes(k.access, var, 4).s == 1
+
+    # staging order: consecutive threads walk the operand's contiguous dimension
+    a_k_fast = not (contiguous(A, "X") and not contiguous(A, "Y"))
+    b_n_fast = not (contiguous(B, "X") and not contiguous(B, "Y"))
+    a_idx = "const int kk = e % 16, mm = e / 16;" if a_k_fast else "const int mm = e % 64, kk = e / 64;"
+    b_idx = "const int nn = e % 64, kb = e / 64;" if b_n_fast else "const int kb = e % 16, nn = e / 16;"
+    full_mk = M % 64 == 0 and K % 16 == 0
+    full_nk = N % 64 == 0 and K % 16 == 0
+    a_val = la if full_mk else f"(gm < ({it}){M} && gk < ({it}){K}) ? ({la}) : 0.0f"
+    b_val = lb if full_nk else f"(gn < ({it}){N} && gk < ({it}){K}) ? ({lb}) : 0.0f"
+    out_guard = "true" if (M % 64 == 0 and N % 64 == 0) else f"om < ({it}){M} && on < ({it}){N}"
     src = f"""extern "C" __global__ void __launch_bounds__(256) {name}({params}) {{
-    __shared__ float As[16][64 + 4];
-    __shared__ float Bs[16][64 + 4];
+    __shared__ __align__(16) float As[16][64 + 4];
+    __shared__ __align__(16) float Bs[16][64 + 4];
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
     const {it} m0 = ({it})blockIdx.y * 64, n0 = ({it})blockIdx.x * 64;
     float acc[4][4];
@@ -710,27 +724,25 @@ def gen_dot_simt(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
         #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
     for ({it} k0 = 0; k0 < ({it}){K}; k0 += 16) {{
+        #pragma unroll
         for (int e = threadIdx.x; e < 16 * 64; e += 256) {{
-            const int kk = e % 16, mm = e / 16;
-            const {it} gm = m0 + mm, gk = k0 + kk;
-            As[kk][mm] = (gm < ({it}){M} && gk < ({it}){K}) ? ({la}) : 0.0f;
-            const int nn = e % 64, kb = e / 64;
-            const {it} gn = n0 + nn, gk2 = k0 + kb;
-            {{ const {it} gk = gk2;
-               Bs[kb][nn] = (gn < ({it}){N} && gk < ({it}){K}) ? ({lb}) : 0.0f; }}
+            {{ {a_idx}
+               const {it} gm = m0 + mm, gk = k0 + kk;
+               As[kk][mm] = {a_val}; }}
+            {{ {b_idx}
+               const {it} gn = n0 + nn, gk = k0 + kb;
+               Bs[kb][nn] = {b_val}; }}
         }}
         __syncthreads();
         #pragma unroll
         for (int kk = 0; kk < 16; ++kk) {{
-            float a[4], b[4];
-            #pragma unroll
-            for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
-            #pragma unroll
-            for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+            const float4 a = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+            const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+            const float av[4] = {{a.x, a.y, a.z, a.w}}, bv[4] = {{b.x, b.y, b.z, b.w}};
             #pragma unroll
             for (int i = 0; i < 4; ++i)
                 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
         }}
         __syncthreads();
     }}
@@ -739,7 +751,7 @@ def gen_dot_simt(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
         #pragma unroll
         for (int j = 0; j < 4; ++j) {{
             const {it} om = m0 + ty * 4 + i, on = n0 + tx * 4 + j;
-            if (om < ({it}){M} && on < ({it}){N}) {{
+            if ({out_guard}) {{
                 const float accv = acc[i][j];
                 {epi}
             }}

@@ -13,6 +13,7 @@ epilogue with ``_x = ty, _y = tx, _global_id = ty * wB + tx``
 """
 from __future__ import annotations
 
+import os
 from typing import Dict, List
 
 from . import codegen, ir
@@ -30,7 +31,8 @@ def use_tensor_cores(dev, M: int, N: int, K: int) -> bool:
     # across independent commands (e.g. per-head projections), does better
     from .tcgen05 import BM, pad, tile_n
     tiles = (pad(M, BM) // BM) * (pad(N, tile_n(N)) // tile_n(N))
-    return tiles >= 64 or (tiles >= 8 and M * N * K >= (1 << 27))
+    min_tiles = int(os.environ.get("AD_TC_MIN_TILES", "64"))
+    return tiles >= min_tiles or (tiles >= 8 and M * N * K >= (1 << 27) and min_tiles <= 64)
 
 
 def single_kernel_spec(dev, cmd, name: str, sizes: Dict[int, int]):

@@ -218,6 +218,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernel-timing", action="store_true",
+                    help="skip the per-kernel isolated timings (loop workloads)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = WORKLOADS[args.workload]
@@ -395,7 +397,7 @@ def bench_loop(args, wl, rank, world, local, td):
     ms = allmax(td, e0.elapsed_ms(e1) / args.steps)
     dev.check_errors()
     per_kernel = np.zeros(len(launches))
-    for i, L in enumerate(launches):
+    for i, L in enumerate(launches if not args.no_kernel_timing else []):
         g = dev.capture_launches([L], 5)
         g.launch(0)
         a, b = ctx.event(True), ctx.event(True)
@@ -408,7 +410,7 @@ def bench_loop(args, wl, rank, world, local, td):
     top = int(np.argmax(per_kernel))
     Lt = launches[top]
     hbm, bf16, peak_kind = peaks()
-    achieved = Lt.spec.bytes_moved / (per_kernel[top] / 1e3) / 1e9
+    achieved = Lt.spec.bytes_moved / (max(per_kernel[top], 1e-9) / 1e3) / 1e9
     feed_bytes = sum(4 * int(np.prod(c.shape)) for c in ir.iter_cmds(loop.proc) if type(c).__name__ == "Feeder")
     value = 1e3 / ms * world
     if rank == 0:
@@ -428,6 +430,7 @@ def bench_loop(args, wl, rank, world, local, td):
                          "note": "latency-bound: kernels of a few microseconds"},
             "per_kernel_ms": [round(float(x), 4) for x in per_kernel],
             "per_kernel_kind": [L.spec.kind for L in launches],
+            "per_kernel_gflop": [round(L.spec.flops / 1e9, 3) for L in launches],
             "clocks": clk.summary(),
             "e2e": {"value": value, "unit": wl["unit"], "h2d_bytes_per_step": feed_bytes,
                     "d2h_bytes_per_step": 0,
