@@ -264,41 +264,115 @@ class RunState:
         return True
 
 
-def find_runs(body: List) -> List[Tuple[int, int, int, int]]:
-    """Maximal runs [i, j) of commands in ``body`` that fuse; returns (i, j, V, R)."""
-    runs = []
-    n = len(body)
-    i = 0
-    while i < n:
-        anchor = None
-        for j in range(i, min(n, i + 4)):
-            c = body[j]
-            if type(c).__name__ in RED:
-                rn = c if type(c).__name__ == "ReduceNode" else c.init_node
-                anchor = tuple(rn.children_shapes[0])
-                break
-            if type(c).__name__ not in ELW:
-                break
-        if anchor is None:
-            i += 1
-            continue
-        V, R = anchor
-        if R % VEC != 0 or R < 32 or R // VEC > 1024 * MAX_CHUNKS:
-            i += 1
-            continue
-        st = RunState(V, R)
-        j = i
-        best = None
-        while j < n and type(body[j]).__name__ in ELW + RED and st.add(body[j]):
-            j += 1
-            if st.n_reduce:
-                best = j
-        if best is not None and best - i >= 2:
-            runs.append((i, best, V, R))
-            i = best
+def _depends_on_run(c, written: Set[int]) -> bool:
+    for n in codegen.chain_nodes(c):
+        for k in n.kargs:
+            if any(km.id in written for km in _kmats(k)):
+                return True
+    return False
+
+
+def _rw(c) -> Tuple[Set[int], Set[int]]:
+    from .memplan import _accesses
+    r, w = _accesses(c)
+    return set(r), set(w)
+
+
+WINDOW = 640    # how far ahead a run looks for dependent commands
+
+
+def _anchor_shape(body: List, i: int, rws) -> Optional[Tuple[int, int]]:
+    c = body[i]
+    k = type(c).__name__
+    if k in RED:
+        rn = c if k == "ReduceNode" else c.init_node
+        return tuple(rn.children_shapes[0])
+    if k not in ELW:
+        return None
+    n_el = math.prod(c.init_node.shape if k == "ElwFuse" else c.shape)
+    w = rws[i][1]
+    for j in range(i + 1, min(len(body), i + WINDOW)):
+        d = body[j]
+        if isinstance(d, ir.ForNode):
+            return None
+        if type(d).__name__ in RED and rws[j][0] & w:
+            rn = d if type(d).__name__ == "ReduceNode" else d.init_node
+            V, R = rn.children_shapes[0]
+            return (V, R) if V * R == n_el or V == n_el else None
+    return None
+
+
+def _fully_connected(c, run_w: Set[int]) -> bool:
+    """Every statement of ``c`` reads something the run (or an earlier statement
+    of ``c`` that does) produced.  Keeps out commands that only partly belong to
+    the run, e.g. the reference's horizontal ElwFuse of all attention heads."""
+    live = set(run_w)
+    live_t: Set[int] = set()
+    for n in codegen.chain_nodes(c):
+        hit = False
+        for k in n.kargs:
+            for km in _kmats(k):
+                hit |= km.id in live
+            if isinstance(k, ir.KMatrix) and k.is_temp and k.id in live_t:
+                hit = True
+        if not hit:
+            return False
+        if n.kres.is_temp:
+            live_t.add(n.kres.id)
         else:
-            i += 1
-    return runs
+            live.add(n.kres.id)
+    return True
+
+
+def grow_run(body: List, rws, i: int) -> Optional[Tuple[List[int], int, int, int]]:
+    """Try to grow a row run from anchor ``body[i]`` (a reduction, or an
+    elementwise command feeding one).  Later commands that read something the
+    run wrote may join.  The run executes at position ``P``: while no skipped
+    command conflicts with the run, members are *sunk* to the newest member
+    (P moves there); once one conflicts (reads what the run writes, or writes
+    what it reads or writes), later candidates must be *hoisted* to P, which
+    needs them not to read what a command skipped after P writes, nor write
+    what one reads or writes.  Independent siblings (the same softmax of other
+    attention heads) are skipped and form their own runs, which the batching
+    pass launches side by side.  Returns (members, P, V, R) or None."""
+    n = len(body)
+    shape = _anchor_shape(body, i, rws)
+    if shape is None:
+        return None
+    V, R = shape
+    if R % VEC != 0 or R < 32 or R // VEC > 1024 * MAX_CHUNKS:
+        return None
+    st = RunState(V, R)
+    if not st.add(body[i]):
+        return None
+    members = [i]
+    P = i
+    run_r, run_w = set(rws[i][0]), set(rws[i][1])
+    skip_r: Set[int] = set()
+    skip_w: Set[int] = set()
+    blocked = False
+    for j in range(i + 1, min(n, i + WINDOW)):
+        d = body[j]
+        if isinstance(d, ir.ForNode):
+            break
+        r, w = rws[j]
+        if type(d).__name__ in ELW + RED and (r & run_w) and _fully_connected(d, run_w):
+            ok = (not blocked) or (not (r & skip_w) and not (w & (skip_r | skip_w)))
+            if ok and st.add(d):
+                members.append(j)
+                run_r |= r
+                run_w |= w
+                if not blocked:
+                    P = j
+                    skip_r, skip_w = set(), set()
+                continue
+        if (r & run_w) or (w & (run_r | run_w)):
+            blocked = True
+        skip_r |= r
+        skip_w |= w
+    if st.n_reduce and len(members) >= 2:
+        return members, P, V, R
+    return None
 
 
 def run_state(cmds, V, R) -> RunState:
@@ -352,30 +426,44 @@ def fuse_rows(proc: ir.Proc) -> ir.Proc:
         for c in seq:
             if type(c).__name__ == "ForNode":
                 rewrite(c.proc)
-        runs = find_runs(seq)
-        if not runs:
-            return
-        replace: Dict[int, object] = {}
-        drop: Set[int] = set()
-        for (i, j, V, R) in runs:
-            cmds = seq[i:j]
-            ps = [pos_of[id(c)] for c in cmds]
-            lo, hi = min(ps), max(ps)
-            kinds = run_kinds(cmds, V, R)
-            internal = set()
-            for b in kinds:
-                if all(lo <= u <= hi for u in uses.get(b, [])):
-                    internal.add(b)
-            rf = RowFused(cmds, V, R, internal, getattr(cmds[0], "program_id", -1))
-            replace[id(cmds[0])] = rf
-            for c in cmds[1:]:
-                drop.add(id(c))
-        new = []
-        for c in body:
-            if id(c) in drop:
+        rws = [(_rw(c) if not isinstance(c, ir.ForNode) else (set(), set())) for c in seq]
+        i = 0
+        changed = False
+        while i < len(seq):
+            if type(seq[i]).__name__ not in ELW + RED:
+                i += 1
                 continue
-            new.append(replace.get(id(c), c))
-        p.procedure = new
+            got = grow_run(seq, rws, i)
+            if got is None:
+                i += 1
+                continue
+            members, P, V, R = got
+            cmds = [seq[m] for m in members]
+            mpos = {pos_of[id(c)] for c in cmds}
+            kinds = run_kinds(cmds, V, R)
+            internal = {b for b in kinds if all(u in mpos for u in uses.get(b, []))}
+            rf = RowFused(cmds, V, R, internal, getattr(cmds[0], "program_id", -1))
+            rr, ww = set(), set()
+            for m in members:
+                rr |= rws[m][0]
+                ww |= rws[m][1]
+            mset = set(members)
+            new_seq, new_rws = [], []
+            for k, c in enumerate(seq):
+                if k == P:
+                    new_seq.append(rf)
+                    new_rws.append((rr, ww))
+                elif k not in mset:
+                    new_seq.append(c)
+                    new_rws.append(rws[k])
+            seq, rws = new_seq, new_rws
+            changed = True
+            # the anchor slot now holds the next command (or the run itself)
+        if not changed:
+            return
+        others = [c for c in body if type(c).__name__ in ("AllocEntry", "DeallocEntry")]
+        p.procedure = [c for c in others if type(c).__name__ == "AllocEntry"] + seq + \
+            [c for c in others if type(c).__name__ == "DeallocEntry"]
 
     rewrite(proc)
     return proc

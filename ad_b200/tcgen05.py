@@ -349,7 +349,9 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
                 #pragma unroll
                 for (int j = 0; j < 32; ++j) tr[lane * 32 + (j ^ lane)] = __uint_as_float(r[j]);
                 __syncwarp();
-                #pragma unroll 4
+                // all 32 rows unrolled: the epilogue's global loads (bias, residuals,
+                // in-place parameters) are issued together instead of 4 at a time
+                #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const IDX om = (IDX)m0 + q * 32 + i;
                     const IDX on = (IDX)n0 + c * 32 + lane;

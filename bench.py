@@ -384,8 +384,9 @@ def bench_loop(args, wl, rank, world, local, td):
     launches = [L for c in body_cmds for L in dev.launches[id(c)]]
     ctx = dev.ctx
     dev._run_proc(proc, dev.run)          # warm-up: W iterations + final Receiver
-    ctx.sync()
     loop.r = range(args.steps)
+    dev._replay_graph(loop)               # captures the graphs for this loop length outside the timing
+    ctx.sync()
     barrier(td)
     e0, e1 = ctx.event(True), ctx.event(True)
     with ClockSampler(local) as clk:
