@@ -713,9 +713,12 @@ def gen_dot_simt(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
     a_val = la if full_mk else f"(gm < ({it}){M} && gk < ({it}){K}) ? ({la}) : 0.0f"
     b_val = lb if full_nk else f"(gn < ({it}){N} && gk < ({it}){K}) ? ({lb}) : 0.0f"
     out_guard = "true" if (M % 64 == 0 and N % 64 == 0) else f"om < ({it}){M} && on < ({it}){N}"
+    nk = (K + 15) // 16
     src = f"""extern "C" __global__ void __launch_bounds__(256) {name}({params}) {{
-    __shared__ __align__(16) float As[16][64 + 4];
-    __shared__ __align__(16) float Bs[16][64 + 4];
+    // double-buffered 16-deep k slices: slice t+1 is fetched into registers
+    // while slice t is multiplied out of shared memory
+    __shared__ __align__(16) float As[2][16][64 + 4];
+    __shared__ __align__(16) float Bs[2][16][64 + 4];
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
     const {it} m0 = ({it})blockIdx.y * 64, n0 = ({it})blockIdx.x * 64;
     float acc[4][4];
@@ -723,27 +726,44 @@ def gen_dot_simt(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
     for (int i = 0; i < 4; ++i)
         #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-    for ({it} k0 = 0; k0 < ({it}){K}; k0 += 16) {{
+    float ra[4], rb[4];
+    auto fetch = [&]({it} k0) {{
         #pragma unroll
-        for (int e = threadIdx.x; e < 16 * 64; e += 256) {{
+        for (int u = 0; u < 4; ++u) {{
+            const int e = threadIdx.x + u * 256;
             {{ {a_idx}
                const {it} gm = m0 + mm, gk = k0 + kk;
-               As[kk][mm] = {a_val}; }}
+               ra[u] = {a_val}; }}
             {{ {b_idx}
                const {it} gn = n0 + nn, gk = k0 + kb;
-               Bs[kb][nn] = {b_val}; }}
+               rb[u] = {b_val}; }}
         }}
-        __syncthreads();
+    }};
+    auto stash = [&](int buf) {{
+        #pragma unroll
+        for (int u = 0; u < 4; ++u) {{
+            const int e = threadIdx.x + u * 256;
+            {{ {a_idx} As[buf][kk][mm] = ra[u]; }}
+            {{ {b_idx} Bs[buf][kb][nn] = rb[u]; }}
+        }}
+    }};
+    fetch(0);
+    stash(0);
+    __syncthreads();
+    for (int t = 0; t < {nk}; ++t) {{
+        const int cur = t & 1;
+        if (t + 1 < {nk}) fetch(({it})(t + 1) * 16);
         #pragma unroll
         for (int kk = 0; kk < 16; ++kk) {{
-            const float4 a = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
-            const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+            const float4 a = *reinterpret_cast<const float4*>(&As[cur][kk][ty * 4]);
+            const float4 b = *reinterpret_cast<const float4*>(&Bs[cur][kk][tx * 4]);
             const float av[4] = {{a.x, a.y, a.z, a.w}}, bv[4] = {{b.x, b.y, b.z, b.w}};
             #pragma unroll
             for (int i = 0; i < 4; ++i)
                 #pragma unroll
                 for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
         }}
+        if (t + 1 < {nk}) stash(cur ^ 1);
         __syncthreads();
     }}
     #pragma unroll
