@@ -39,7 +39,7 @@ WORKLOADS = {
             "data": "Feeder of np.full((2,255), 0.2); weights from np.random.seed(0) randn (reference init)"},
     "enc": {"case": "enc_4_32_128_512_8_2048_100",
             "metric": "encoder train steps/s (4 layers, d512, 8 heads, ff2048, S128, B32, fp32, SGD)",
-            "unit": "steps/s", "loop": True, "cpu_iters": 1,
+            "unit": "steps/s", "loop": True, "cpu_iters": 1, "dp": True, "global_batch": 32,
             "data": "synthetic: x ~ N(0,1) [4096, 512] seed 0 via Feeder; Xavier-uniform weights (seeded)"},
     "enc_small": {"case": "enc_1_8_128_512_8_2048_100",
                   "metric": "encoder train steps/s (1 layer, d512, 8 heads, ff2048, S128, B8, fp32, SGD)",
@@ -375,9 +375,18 @@ def bench_loop(args, wl, rank, world, local, td):
     from ad_b200 import ir
     from ad_b200.device import CudaB200Device
     from ad_b200.fixtures import load_case, set_loop_count
-    p, meta = load_case(wl["case"])
+    case = wl["case"]
+    dp = None
+    if world > 1 and wl.get("dp"):
+        # data parallel: this rank's shard of the global batch, gradients summed with NCCL
+        case = f"{case}_p{world}"
+        from ad_b200 import dist
+        box = [dist.nccl_unique_id() if rank == 0 else None]
+        td.broadcast_object_list(box, src=0)
+        dp = (rank, world, box[0])
+    p, meta = load_case(case, rank=rank)
     set_loop_count(p, args.warmup)
-    dev = CudaB200Device(local)
+    dev = CudaB200Device(local, dp=dp)
     proc = dev.prepare(p)
     loop = next(c for c in proc.procedure if isinstance(c, ir.ForNode))
     body_cmds = [c for c in loop.proc.procedure if id(c) in dev.launches]
@@ -413,16 +422,18 @@ def bench_loop(args, wl, rank, world, local, td):
     hbm, bf16, peak_kind = peaks()
     achieved = Lt.spec.bytes_moved / (max(per_kernel[top], 1e-9) / 1e3) / 1e9
     feed_bytes = sum(4 * int(np.prod(c.shape)) for c in ir.iter_cmds(loop.proc) if type(c).__name__ == "Feeder")
-    value = 1e3 / ms * world
+    value = 1e3 / ms * (1 if dp else world)
     if rank == 0:
         line = {
             "metric": wl["metric"], "value": value, "unit": wl["unit"], "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": wl["data"],
-            "config": {"workload": wl["case"], "kernels_per_step": len(launches),
+            "scaling": "strong" if dp else "weak", "vs_baseline": None, "dtype": "f32", "data": wl["data"],
+            "config": {"workload": case, "kernels_per_step": len(launches),
+                       "global_batch": wl.get("global_batch"),
                        "step": "one ForNode iteration as a CUDA graph (Feeder H2D + kernels)",
                        "l2": "working set fits in L2 (tiny model); launch-latency bound",
-                       "parallelism": f"replicas x{world}"},
+                       "parallelism": (f"data parallel x{world} (NCCL all-reduce of gradients)" if dp
+                                       else f"replicas x{world}")},
             "gpu_launches": len(launches) * args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": None, "peak_kind": peak_kind,
