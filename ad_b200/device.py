@@ -151,6 +151,10 @@ class CudaB200Device:
         kind = type(cmd).__name__
         sizes = {b: s.size for b, s in self.slots.items()}
         name = f"k_{kind}"
+        if kind == "Batched" and type(cmd.cmds[0]).__name__ in DOT and \
+                self._single_spec(cmd.cmds[0], sizes) is None:
+            from . import tcgen05
+            return tcgen05.plan_group(self, cmd.cmds, name, sizes)
         if kind == "Batched":
             from . import batch
             members = [self._single_spec(c, sizes) for c in cmd.cmds]
@@ -175,8 +179,10 @@ class CudaB200Device:
     def _upload_table(self, spec) -> int:
         """Device table of pointer parameters of a batched launch (instance-major)."""
         rows = []
-        for bufs, err in spec.extra["table"]:
-            row = [self.view_ptr(v) for v in bufs] + ([self.err_ptr] if err else [])
+        for entry in spec.extra["table"]:
+            bufs, err = entry[0], entry[1]
+            pre, post = (entry[2], entry[3]) if len(entry) > 2 else ([], [])
+            row = list(pre) + [self.view_ptr(v) for v in bufs] + ([self.err_ptr] if err else []) + list(post)
             assert len(row) == spec.extra["nparam"]
             rows += row
         a = np.asarray(rows, dtype=np.uint64)
@@ -222,7 +228,8 @@ class CudaB200Device:
             ls = []
             for s in specs:
                 if "table" in s.extra:
-                    ls.append(Launch(s, self.kernels[s.src], [self._upload_table(s)], {}))
+                    ls.append(Launch(s, self.kernels[s.src], [self._upload_table(s)],
+                                     {"prefix": s.extra.get("prefix", []), "suffix": s.extra.get("suffix", [])}))
                     continue
                 ptrs = [self.view_ptr(v) for v in s.buffers]
                 ls.append(Launch(s, self.kernels[s.src], ptrs, s.extra))
@@ -386,6 +393,9 @@ class CudaB200Device:
                 if type(c).__name__ not in ir.COMPUTE_KINDS:
                     return None
                 sp = self._single_spec(c, sizes)
+                if sp is None and type(c).__name__ in DOT:
+                    from . import gemm
+                    return gemm.tc_signature(self, c)
                 return None if sp is None else sp.src
             batch.batch_proc(proc, signature)
         self.proc = proc

@@ -13,7 +13,6 @@ epilogue with ``_x = ty, _y = tx, _global_id = ty * wB + tx``
 """
 from __future__ import annotations
 
-import os
 from typing import Dict, List
 
 from . import codegen, ir
@@ -25,14 +24,10 @@ def use_tensor_cores(dev, M: int, N: int, K: int) -> bool:
         return False
     if mode == "tc":
         return True
-    if M * N * K < (1 << 21) or min(M, N) < 16 or K < 8:
-        return False
-    # too few output tiles to occupy the GPU: the CUDA-core kernel, which batches
-    # across independent commands (e.g. per-head projections), does better
-    from .tcgen05 import BM, pad, tile_n
-    tiles = (pad(M, BM) // BM) * (pad(N, tile_n(N)) // tile_n(N))
-    min_tiles = int(os.environ.get("AD_TC_MIN_TILES", "64"))
-    return tiles >= min_tiles or (tiles >= 8 and M * N * K >= (1 << 27) and min_tiles <= 64)
+    # small products (per-(sequence, head) attention blocks): the CUDA-core
+    # kernels, batched across commands, beat a split + tensor-core pipeline.
+    # Larger ones fill the GPU through grouping and split-K.
+    return M * N * K >= (1 << 22) and min(M, N) >= 16 and K >= 8
 
 
 def single_kernel_spec(dev, cmd, name: str, sizes: Dict[int, int]):
@@ -42,6 +37,17 @@ def single_kernel_spec(dev, cmd, name: str, sizes: Dict[int, int]):
     if use_tensor_cores(dev, M, N, K):
         return None
     return plan_dot(dev, cmd, name, sizes)[0]
+
+
+def tc_signature(dev, cmd) -> str:
+    """Commands with equal signatures can share one grouped tensor-core launch:
+    same shapes, operand accesses and epilogue, only their buffers differ."""
+    from . import tcgen05
+    dn, M, N, K = codegen.dot_shape(cmd)
+    bn = tcgen05.tile_n(N)
+    (sa, sb), _ = tcgen05._operands([cmd], "k")
+    g = tcgen05.gen_gemm(cmd, "k", M, N, K, bn, tcgen05.stages_for(bn))
+    return "\n".join(["tc", sa[0][0].src, sb[0][0].src, g.src])
 
 
 def plan_dot(dev, cmd, name: str, sizes: Dict[int, int]) -> List[codegen.KernelSpec]:
@@ -56,14 +62,18 @@ def plan_dot(dev, cmd, name: str, sizes: Dict[int, int]) -> List[codegen.KernelS
 
 def setup_scratch(dev, proc: ir.Proc) -> None:
     """Scratch for the tensor-core path (split operands), sized for the largest dot."""
+    from . import tcgen05
     dev.scratch = {}
     need = 0
     for c in ir.iter_cmds(proc):
-        if type(c).__name__ in ("DotProdNode", "DPElwFuse"):
+        if type(c).__name__ == "Batched" and type(c.cmds[0]).__name__ in ("DotProdNode", "DPElwFuse"):
+            dn, M, N, K = codegen.dot_shape(c.cmds[0])
+            if use_tensor_cores(dev, M, N, K):
+                need = max(need, tcgen05.group_scratch_bytes(c.cmds, dev.ctx.sm_count))
+        elif type(c).__name__ in ("DotProdNode", "DPElwFuse"):
             dn, M, N, K = codegen.dot_shape(c)
             if use_tensor_cores(dev, M, N, K):
-                from . import tcgen05
-                need = max(need, tcgen05.scratch_bytes(M, N, K))
+                need = max(need, tcgen05.scratch_bytes(M, N, K, dev.ctx.sm_count))
     if need:
         base = dev.ctx.malloc(need)
         dev.scratch_allocs.append(base)

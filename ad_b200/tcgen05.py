@@ -54,10 +54,24 @@ def tile_n(N: int) -> int:
     return 256 if N > 128 else (128 if N > 64 else 64)
 
 
-def scratch_bytes(M: int, N: int, K: int) -> int:
+def scratch_bytes(M: int, N: int, K: int, sm_count: int = 148) -> int:
+    return _layout_bytes(M, N, K, 1, 1, 1, sm_count)
+
+
+def _ksplit_for(M: int, N: int, K: int, n_inst: int, sm_count: int) -> int:
+    bn = tile_n(N)
+    units = n_inst * (pad(M, BM) // BM) * (pad(N, bn) // bn)
+    return choose_ksplit(units, pad(K, BK) // BKF, sm_count)
+
+
+def _layout_bytes(M: int, N: int, K: int, nA: int, nB: int, n_inst: int, sm_count: int) -> int:
+    """Scratch of one (grouped) dot: stacked hi/lo operands, then the split-K
+    partial sums."""
     bn = tile_n(N)
     Mp, Np, Kp = pad(M, BM), pad(N, bn), pad(K, BK)
-    return 2 * 4 * (Mp * Kp + Np * Kp) + 4096
+    ks = _ksplit_for(M, N, K, n_inst, sm_count)
+    ws = 4 * n_inst * ks * M * N if ks > 1 else 0
+    return 2 * 4 * (nA * Mp * Kp + nB * Np * Kp) + ws + 4096
 
 
 # ---------------------------------------------------------------- split kernel
@@ -194,6 +208,16 @@ __device__ __forceinline__ void tile_of(int t, int& m_blk, int& n_blk) {
     n_blk = r / gsz;
 }
 
+__device__ __forceinline__ void decode(int t, int& inst, int& ks, int& m_blk, int& n_blk) {
+    // instances of a grouped launch are consecutive ranges of KSPLIT x M_BLOCKS x N_BLOCKS
+    // work units; ks = which slice of the K blocks this unit accumulates
+    constexpr int PER = M_BLOCKS * N_BLOCKS;
+    inst = t / (PER * KSPLIT);
+    const int r = t - inst * (PER * KSPLIT);
+    ks = r / PER;
+    tile_of(r - ks * PER, m_blk, n_blk);
+}
+
 // Persistent, warp-specialised: warp 0 = TMA producer, warp 1 = MMA issuer,
 // warps 2..9 = epilogue (TMEM lane quarter = warp % 4, column half = (warp - 2) / 4).
 // Two TMEM accumulators (2 x BN columns) let the epilogue of one tile overlap the
@@ -203,7 +227,7 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
     const __grid_constant__ TmapT tBh, const __grid_constant__ TmapT tBl,
     PARAMS int* __restrict__ err)
 {
-    constexpr int BN = TILE_N, STAGES = NSTAGES, KB = KBLOCKS, NUM_TILES = M_BLOCKS * N_BLOCKS;
+    constexpr int BN = TILE_N, STAGES = NSTAGES, KB = KBLOCKS, NUM_TILES = NUM_INST * M_BLOCKS * N_BLOCKS * KSPLIT;
     constexpr unsigned A_BYTES = 128 * ROWB, B_BYTES = BN * ROWB;
     constexpr unsigned STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     constexpr int EPI_WARPS = 8;
@@ -243,9 +267,11 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
             // ---------------- TMA producer
             int it = 0;
             for (int t = blockIdx.x; t < NUM_TILES && !*abort_flag; t += gridDim.x) {
-                int mb, nb;
-                tile_of(t, mb, nb);
-                for (int kb = 0; kb < KB; ++kb, ++it) {
+                int inst, ks, mb, nb;
+                decode(t, inst, ks, mb, nb);
+                const int arow = A_ROW + mb * 128, brow = B_ROW + nb * BN;
+                const int kb0 = ks * KB / KSPLIT, kb1 = (ks + 1) * KB / KSPLIT;
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % STAGES;
                     if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, abort_flag)) {
                         if (!*abort_flag) atomicExch(err, 1);
@@ -254,10 +280,10 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
                     }
                     unsigned char* st = smem + s * STAGE_BYTES;
                     mbar_expect_tx(&full[s], STAGE_BYTES);
-                    tma_load_2d(st, &tAh, &full[s], kb * BKF, mb * 128);
-                    tma_load_2d(st + A_BYTES, &tAl, &full[s], kb * BKF, mb * 128);
-                    tma_load_2d(st + 2 * A_BYTES, &tBh, &full[s], kb * BKF, nb * BN);
-                    tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tBl, &full[s], kb * BKF, nb * BN);
+                    tma_load_2d(st, &tAh, &full[s], kb * BKF, arow);
+                    tma_load_2d(st + A_BYTES, &tAl, &full[s], kb * BKF, arow);
+                    tma_load_2d(st + 2 * A_BYTES, &tBh, &full[s], kb * BKF, brow);
+                    tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tBl, &full[s], kb * BKF, brow);
                 }
             }
             if (*abort_flag) {
@@ -283,7 +309,10 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const unsigned d = tmem + (unsigned)(a * BN);
                 bool ok = true;
-                for (int kb = 0; kb < KB; ++kb, ++it) {
+                int inst, ks, mb, nb;
+                decode(t, inst, ks, mb, nb);
+                const int kb0 = ks * KB / KSPLIT, kb1 = (ks + 1) * KB / KSPLIT;
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % STAGES;
                     if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) {
                         if (!*abort_flag) atomicExch(err, 2);
@@ -298,7 +327,7 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
                     #pragma unroll
                     for (int k8 = 0; k8 < BKF / 8; ++k8) {
                         const unsigned long long adv = (unsigned long long)(k8 * 32) >> 4;  // 8 fp32 = 32 bytes
-                        const unsigned first = (kb > 0 || k8 > 0) ? 1u : 0u;
+                        const unsigned first = (kb > kb0 || k8 > 0) ? 1u : 0u;
                         mma_tf32(d, ah + adv, bh + adv, IDESC, first);
                         mma_tf32(d, ah + adv, bl + adv, IDESC, 1u);
                         mma_tf32(d, al + adv, bh + adv, IDESC, 1u);
@@ -324,9 +353,10 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            int mb, nb;
-            tile_of(t, mb, nb);
+            int inst, ks, mb, nb;
+            decode(t, inst, ks, mb, nb);
             const int m0 = mb * 128, n0 = nb * BN;
+            EPI_PTRS
             #pragma unroll 1
             for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
                 unsigned r[32];
@@ -375,27 +405,107 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
 """
 
 
-def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int, sm_count: int = 148) -> KernelSpec:
+def choose_ksplit(units: int, kblocks: int, sm_count: int) -> int:
+    """K slices per output tile: minimise waves x (K blocks per slice + pipeline
+    fill), at least 4 K blocks per slice, a small cost per extra slice for the
+    partial sums' round trip."""
+    best, best_cost = 1, None
+    for s_ in range(1, min(32, kblocks // 4) + 1):
+        waves = -(-units * s_ // sm_count)
+        cost = waves * (-(-kblocks // s_) + 6) + (2 if s_ > 1 else 0)
+        if best_cost is None or cost < best_cost:
+            best, best_cost = s_, cost
+    return best
+
+
+def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int, sm_count: int = 148,
+             n_inst: int = 1, ksplit: int = 1) -> KernelSpec:
+    """The GEMM kernel of dot command ``c``.  With ``n_inst > 1`` it is a grouped
+    launch over ``n_inst`` commands whose kernels differ only in their pointers:
+    the kernel then takes a device table, per instance ``[A row base, B row base,
+    epilogue pointers...]`` (row bases index the stacked split operands).
+    With ``ksplit > 1`` each output tile is computed as ``ksplit`` partial sums
+    over consecutive K ranges, stored raw to ``ad_ws[inst][slice][M][N]``; the
+    fused epilogue then runs in ``gen_splitk_epilogue``'s kernel."""
     rng = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
     it = index_type(_epi_only(c), rng)
     bufs, em = codegen.make_emitter(c, it)
-    epi = dot_epilogue(c, em, it, "accv", {"X": "om", "Y": "on", "G": f"(om * ({it}){N} + on)"})
-    epi = "\n                    ".join(epi.split("\n"))
-    params = "".join(f"float* __restrict__ p{i}, " for i in range(len(bufs)))
+    tabw = 2 + len(bufs)
+    if ksplit == 1:
+        epi = dot_epilogue(c, em, it, "accv", {"X": "om", "Y": "on", "G": f"(om * ({it}){N} + on)"})
+        epi = "\n                    ".join(epi.split("\n"))
+    else:
+        epi = (f"ad_ws[((long long)(inst * {ksplit} + ks) * {M} + (long long)om) * {N} + (long long)on] = accv;")
+    if n_inst == 1:
+        params = ("".join(f"float* __restrict__ p{i}, " for i in range(len(bufs))) if ksplit == 1
+                  else "float* __restrict__ ad_ws, ")
+        a_row, b_row, epi_ptrs = "0", "0", ""
+    else:
+        params = "const unsigned long long* __restrict__ ad_tab, " + \
+            ("float* __restrict__ ad_ws, " if ksplit > 1 else "")
+        a_row = f"(int)ad_tab[(unsigned)inst * {tabw}u]"
+        b_row = f"(int)ad_tab[(unsigned)inst * {tabw}u + 1u]"
+        epi_ptrs = "" if ksplit > 1 else "\n            ".join(
+            f"float* __restrict__ p{i} = reinterpret_cast<float*>(ad_tab[(unsigned)inst * {tabw}u + {2 + i}u]);"
+            for i in range(len(bufs)))
     kb = pad(K, BK) // BKF
     mblk, nblk = pad(M, BM) // BM, pad(N, bn) // bn
     src = (GEMM_TEMPLATE.replace("NAME", name).replace("PARAMS", params).replace("TILE_N", str(bn))
            .replace("NSTAGES", str(stages)).replace("KBLOCKS", str(kb)).replace("GROUP_M", str(GROUP_M))
            .replace("ROWB", str(BKF * 4)).replace("SWZ", "2" if BKF == 32 else "4").replace("BKF", str(BKF))
+           .replace("NUM_INST", str(n_inst)).replace("KSPLIT", str(ksplit))
+           .replace("A_ROW", a_row).replace("B_ROW", b_row).replace("EPI_PTRS", epi_ptrs)
            .replace("M_BLOCKS", str(mblk)).replace("N_BLOCKS", str(nblk))
            .replace("IDX", it).replace("M_DIM", str(M)).replace("N_DIM", str(N)).replace("EPILOGUE", epi))
     stage_bytes = 2 * 128 * BKF * 4 + 2 * bn * BKF * 4
     smem = stages * stage_bytes + 8 * 4096 + 1024 + 256
-    grid = (min(mblk * nblk, sm_count), 1, 1)
+    grid = (min(n_inst * mblk * nblk * ksplit, sm_count), 1, 1)
     rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
     epi_bytes = codegen.written_reads_bytes(_epi_only(c), rngw, {})
-    return KernelSpec(name, src, bufs, grid, (320, 1, 1), smem, "gemm_tcgen05",
-                      4 * (M * K + K * N) + epi_bytes, 2 * M * N * K)
+    if ksplit > 1:
+        bufs = []
+        epi_bytes = 4 * ksplit * M * N
+    spec = KernelSpec(name, src, bufs, grid, (320, 1, 1), smem, "gemm_tcgen05",
+                      n_inst * (4 * (M * K + K * N) + epi_bytes), n_inst * 2 * M * N * K)
+    spec.extra["tabw"] = tabw
+    return spec
+
+
+def gen_splitk_epilogue(c, name: str, M: int, N: int, ksplit: int, n_inst: int = 1) -> KernelSpec:
+    """Sum the ``ksplit`` partial products of each output in slice order and run
+    the command's fused epilogue (dp_elw_fuse.py:11-65 semantics).  Grouped: one
+    ``blockIdx.z`` per instance, pointers from the GEMM's table."""
+    rng = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
+    it = index_type(_epi_only(c), rng)
+    bufs, em = codegen.make_emitter(c, it)
+    tabw = 2 + len(bufs)
+    epi = dot_epilogue(c, em, it, "accv", {"X": "om", "Y": "on", "G": f"(om * ({it}){N} + on)"})
+    if n_inst == 1:
+        params = "".join(f"float* __restrict__ p{i}, " for i in range(len(bufs)))
+        ptrs = ""
+    else:
+        params = "const unsigned long long* __restrict__ ad_tab, "
+        ptrs = "\n    ".join(
+            f"float* __restrict__ p{i} = reinterpret_cast<float*>(ad_tab[(unsigned)inst * {tabw}u + {2 + i}u]);"
+            for i in range(len(bufs)))
+    src = f"""extern "C" __global__ void __launch_bounds__(256) {name}({params}const float* __restrict__ ad_ws) {{
+    const int inst = blockIdx.z;
+    const long long e = (long long)blockIdx.x * 256 + threadIdx.x;
+    if (e >= {M * N}ll) return;
+    {ptrs}
+    const {it} om = ({it})(e / {N}), on = ({it})(e % {N});
+    const float* w = ad_ws + (long long)inst * {ksplit * M * N}ll + e;
+    float accv = 0.0f;
+    #pragma unroll
+    for (int s = 0; s < {ksplit}; ++s) accv += w[(long long)s * {M * N}ll];
+    {epi}
+}}
+"""
+    rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
+    epi_bytes = codegen.written_reads_bytes(_epi_only(c), rngw, {})
+    spec = KernelSpec(name, src, bufs if n_inst == 1 else [], (-(-M * N // 256), 1, n_inst), (256, 1, 1), 0,
+                      "splitk_epilogue", n_inst * (4 * ksplit * M * N + epi_bytes))
+    return spec
 
 
 class _EpiView:
@@ -414,27 +524,94 @@ def _epi_only(c):
 
 
 def plan(dev, cmd, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
-    from . import runtime as rt
-    dn, M, N, K = dot_shape(cmd)
-    A, B = dn.kargs
+    return plan_group(dev, [cmd], name, sizes)
+
+
+def _operands(cmds, name: str):
+    """Split specs of every command's A and B, and the distinct operands among
+    them: commands reading the same data through the same access (the shared
+    input of per-head projections) share one split."""
+    dn, M, N, K = dot_shape(cmds[0])
     bn = tile_n(N)
-    stages = stages_for(bn)
     Mp, Np, Kp = pad(M, BM), pad(N, bn), pad(K, BK)
+    out = []
+    for which, rows, rows_p, rv, kv in ((0, M, Mp, "X", "Y"), (1, N, Np, "Y", "X")):
+        specs, index, uniq = [], [], {}
+        for c in cmds:
+            sp = gen_split(dot_shape(c)[0].kargs[which], name + ("_splitA" if which == 0 else "_splitB"),
+                           rows, K, rows_p, Kp, rv, kv)
+            key = (sp.src, tuple(sp.buffers))
+            if key not in uniq:
+                uniq[key] = len(specs)
+                specs.append(sp)
+            index.append(uniq[key])
+        out.append((specs, index))
+    return out, (M, N, K, bn, Mp, Np, Kp)
+
+
+def group_scratch_bytes(cmds, sm_count: int = 148) -> int:
+    (sa, sb), (M, N, K, bn, Mp, Np, Kp) = _operands(cmds, "k")
+    return _layout_bytes(M, N, K, len(sa[0]), len(sb[0]), len(cmds), sm_count)
+
+
+def _split_launch(specs, name: str, hi: int, lo: int, stride: int) -> KernelSpec:
+    """One launch splitting every distinct operand: operand u goes to rows
+    ``[u * rows_p, (u + 1) * rows_p)`` of the stacked hi/lo arrays."""
+    if len(specs) == 1:
+        sp = specs[0]
+        sp.extra["suffix"] = [ctypes.c_uint64(hi), ctypes.c_uint64(lo)]
+        return sp
+    from .batch import batched_source
+    first = specs[0]
+    src, nparam = batched_source(first.src, name)
+    sp = KernelSpec(name, src, [], (first.grid[0], first.grid[1], len(specs)), first.block, first.smem,
+                    "split_batched", sum(x.bytes_moved for x in specs))
+    sp.extra["table"] = [(x.buffers, False, [], [hi + u * stride, lo + u * stride]) for u, x in enumerate(specs)]
+    sp.extra["nparam"] = nparam
+    return sp
+
+
+def plan_group(dev, cmds, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
+    """Split + GEMM launches for one dot command, or for a group of dot commands
+    with identical kernels (same shapes, accesses and epilogue; different
+    buffers) as one grouped launch each."""
+    from . import runtime as rt
+    ((sa, ia), (sb, ib)), (M, N, K, bn, Mp, Np, Kp) = _operands(cmds, name)
+    stages = stages_for(bn)
+    nA, nB = len(sa), len(sb)
     base = dev.scratch_base
-    a_hi, a_lo = base, base + 4 * Mp * Kp
-    b_hi, b_lo = a_lo + 4 * Mp * Kp, a_lo + 4 * Mp * Kp + 4 * Np * Kp
-    sa = gen_split(A, name + "_splitA", M, K, Mp, Kp, "X", "Y")
-    sb = gen_split(B, name + "_splitB", N, K, Np, Kp, "Y", "X")
-    sa.extra["suffix"] = [ctypes.c_uint64(a_hi), ctypes.c_uint64(a_lo)]
-    sb.extra["suffix"] = [ctypes.c_uint64(b_hi), ctypes.c_uint64(b_lo)]
-    g = gen_gemm(cmd, name + "_tc", M, N, K, bn, stages, dev.ctx.sm_count)
+    a_hi, a_lo = base, base + 4 * nA * Mp * Kp
+    b_hi = a_lo + 4 * nA * Mp * Kp
+    b_lo = b_hi + 4 * nB * Np * Kp
+    split_a = _split_launch(sa, name + "_splitA_x", a_hi, a_lo, 4 * Mp * Kp)
+    split_b = _split_launch(sb, name + "_splitB_x", b_hi, b_lo, 4 * Np * Kp)
+    n = len(cmds)
+    sm = dev.ctx.sm_count
+    ks = _ksplit_for(M, N, K, n, sm)
+    ws = b_lo + 4 * nB * Np * Kp
+    g = gen_gemm(cmds[0], name + ("_tc" if n == 1 else "_tcx"), M, N, K, bn, stages, sm, n, ks)
     sw = BKF * 4
-    maps = [rt.tmap_2d(a_hi, Mp, Kp, 4 * Kp, 128, BKF, 4, sw), rt.tmap_2d(a_lo, Mp, Kp, 4 * Kp, 128, BKF, 4, sw),
-            rt.tmap_2d(b_hi, Np, Kp, 4 * Kp, bn, BKF, 4, sw), rt.tmap_2d(b_lo, Np, Kp, 4 * Kp, bn, BKF, 4, sw)]
+    maps = [rt.tmap_2d(a_hi, nA * Mp, Kp, 4 * Kp, 128, BKF, 4, sw), rt.tmap_2d(a_lo, nA * Mp, Kp, 4 * Kp, 128, BKF, 4, sw),
+            rt.tmap_2d(b_hi, nB * Np, Kp, 4 * Kp, bn, BKF, 4, sw), rt.tmap_2d(b_lo, nB * Np, Kp, 4 * Kp, bn, BKF, 4, sw)]
     g.extra["prefix"] = [ctypes.create_string_buffer(m, 128) for m in maps]
-    g.extra["suffix"] = [ctypes.c_uint64(dev.err_ptr)]
-    g.flops = 2 * M * N * K
-    return [sa, sb, g]
+    g.extra["suffix"] = ([ctypes.c_uint64(ws)] if ks > 1 else []) + [ctypes.c_uint64(dev.err_ptr)]
+    specs = [split_a, split_b, g]
+    rows = []
+    if n > 1:
+        for i, c in enumerate(cmds):
+            bufs, _ = codegen.make_emitter(c, "int")
+            rows.append((bufs, False, [ia[i] * Mp, ib[i] * Np], []))
+        g.buffers = []
+        g.extra["table"] = rows
+        g.extra["nparam"] = g.extra["tabw"]
+    if ks > 1:
+        e = gen_splitk_epilogue(cmds[0], name + ("_ske" if n == 1 else "_skex"), M, N, ks, n)
+        e.extra["suffix"] = [ctypes.c_uint64(ws)]
+        if n > 1:
+            e.extra["table"] = rows
+            e.extra["nparam"] = g.extra["tabw"]
+        specs.append(e)
+    return specs
 
 
 # ---------------------------------------------------------------- tensor-pipe peak probe

@@ -126,6 +126,72 @@ def test_batching_groups_attention_blocks():
     assert sizes and max(sizes) == 64
 
 
+def test_grouped_tensor_core_dots():
+    """Same-kernel dot commands of one dependency level become one grouped
+    tcgen05 launch; operands read by every member (the layer input of the
+    per-head projections) are split once."""
+    from ad_b200.device import CudaB200Device
+    p, _ = load_case("enc_1_8_128_512_8_2048_100")
+    d = CudaB200Device(gemm="tc")
+    d.prepare(p)
+    groups = {}
+    for ls in d.launches.values():
+        kinds = [L.spec.kind for L in ls]
+        if "gemm_tcgen05" in kinds:
+            g = ls[kinds.index("gemm_tcgen05")].spec
+            if "table" in g.extra:
+                groups[len(g.extra["table"])] = (kinds[0], kinds[1])
+    d.close()
+    assert max(groups) == 64
+    assert groups[24] == ("split", "split_batched")
+
+
+@pytest.mark.parametrize("shape,n", [((512, 64, 4096), 1), ((512, 64, 4096), 6), ((640, 200, 3000), 3)])
+def test_split_k_dots(shape, n):
+    """Dots with few output tiles and a long K run as split-K partial sums plus
+    a fused epilogue kernel; single and grouped, ragged shapes included."""
+    from ad_b200 import tcgen05
+    M, N, K = shape
+    assert tcgen05._ksplit_for(M, N, K, n, 148) > 1
+    rng = np.random.default_rng(7)
+    A = [rng.standard_normal((M, K)).astype(np.float32) for _ in range(n)]
+    B = [rng.standard_normal((K, N)).astype(np.float32) for _ in range(n)]
+    got = _run_dots(A, B)
+    for a, b, g in zip(A, B, got):
+        ref = a.astype(np.float64) @ b.astype(np.float64)
+        bound = 1e-4 * (np.abs(a).astype(np.float64) @ np.abs(b).astype(np.float64)) + 1e-5
+        assert np.all(np.abs(g - ref) <= bound)
+
+
+def _run_dots(A, B):
+    """Independent ``C_i = A_i @ B_i`` commands (sigmoid-free DotProd nodes) in one proc."""
+    from ad_b200 import ir
+    from ad_b200.device import CudaB200Device
+    cmds, outs, ids = [], [], 1
+    allocs = []
+    for a, b in zip(A, B):
+        M, K = a.shape
+        N = b.shape[1]
+        ia, ib, ic = ids, ids + 1, ids + 2
+        ids += 3
+        allocs += [ir.AllocEntry(ia, M * K, a.reshape(-1), False), ir.AllocEntry(ib, K * N, b.reshape(-1), False),
+                   ir.AllocEntry(ic, M * N, None, False)]
+        ka = ir.KMatrix(ia, ir.Bin("Add", ir.Bin("Mult", ir.Xv(), ir.Const(K)), ir.Yv()), [M, K])
+        kb = ir.KMatrix(ib, ir.Bin("Add", ir.Bin("Mult", ir.Xv(), ir.Const(N)), ir.Yv()), [K, N])
+        kc = ir.KMatrix(ic, ir.Gid(), [M, N])
+        cmds.append(ir.DotProdNode(1000 + ids, [ka, kb], kc, [M, N], [[M, K], [K, N]]))
+        outs.append(kc)
+    rec = ir.Receiver(999, outs, "out")
+    proc = ir.Proc(allocs + cmds + [rec])
+    d = CudaB200Device(gemm="tc")
+    try:
+        d.execute(proc)
+        got = d.last_received
+    finally:
+        d.close()
+    return got
+
+
 def test_encoder_layer_sgd_step():
     """Config-4 layer shape (d512, 8 heads, ff2048, S128), batch 8, loss = sum(out):
     parameters after one SGD step vs the oracle, rel 1e-3.  With this loss every
@@ -136,11 +202,11 @@ def test_encoder_layer_sgd_step():
         np.testing.assert_allclose(g, w, rtol=1e-3, atol=1e-4)
 
 
-@pytest.mark.parametrize("batch", [True, False])
-def test_encoder_layer_sgd_steps_well_conditioned(batch):
+@pytest.mark.parametrize("batch,gemm", [(True, "auto"), (False, "auto"), (True, "tc")])
+def test_encoder_layer_sgd_steps_well_conditioned(batch, gemm):
     """Same layer with loss = sum(out * R), R ~ N(0,1) fixed: parameters after 3 SGD
     steps vs the oracle, rel 1e-3 (batched attention kernels, row-fused
     LayerNorm/softmax, tensor-core FFN, CUDA-graph loop replay)."""
-    got, want, _ = both("encdy_1_8_128_512_8_2048_3", loops=3, batch=batch)
+    got, want, _ = both("encdy_1_8_128_512_8_2048_3", loops=3, batch=batch, gemm=gemm)
     for g, w in zip(got, want):
         np.testing.assert_allclose(g, w, rtol=1e-3, atol=1e-4)
