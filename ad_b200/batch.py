@@ -65,33 +65,118 @@ def schedule(body: List, signature: Callable[[object], Optional[str]]) -> List:
     return out
 
 
+def _edges(cmds: List) -> List[Set[int]]:
+    """Predecessors of each command: read-after-write, write-after-read and
+    write-after-write on buffer ids; host commands in their original order."""
+    preds: List[Set[int]] = []
+    last_write: Dict[int, int] = {}
+    readers: Dict[int, List[int]] = {}      # buffer -> readers since its last write
+    last_host = -1
+    for i, c in enumerate(cmds):
+        r, w = _rw(c)
+        p: Set[int] = set()
+        for b in r:
+            if b in last_write:
+                p.add(last_write[b])
+        for b in w:
+            if b in last_write:
+                p.add(last_write[b])
+            p.update(readers.get(b, ()))
+        if type(c).__name__ in HOST:
+            if last_host >= 0:
+                p.add(last_host)
+            last_host = i
+        p.discard(i)
+        preds.append(p)
+        for b in r:
+            readers.setdefault(b, []).append(i)
+        for b in w:
+            last_write[b] = i
+            readers[b] = []
+    return preds
+
+
+def _levels(cmds: List, signature) -> List[int]:
+    """A level per command such that every predecessor sits on a lower level,
+    within the critical-path depth, chosen so that commands with equal
+    signatures share levels: each command may go anywhere in its window
+    [as soon as possible, as late as possible]; repeatedly the (signature,
+    level) covering the most unplaced commands is fixed and the windows of
+    their predecessors and successors narrowed, until no two unplaced commands
+    of one signature can share a level; the rest take their earliest level."""
+    n = len(cmds)
+    preds = _edges(cmds)
+    succs: List[List[int]] = [[] for _ in range(n)]
+    for i, ps in enumerate(preds):
+        for j in ps:
+            succs[j].append(i)
+    lo = [0] * n
+    for i in range(n):
+        for j in preds[i]:
+            lo[i] = max(lo[i], lo[j] + 1)
+    depth = max(lo) if n else 0
+    hi = [depth] * n
+    for i in range(n - 1, -1, -1):
+        for j in succs[i]:
+            hi[i] = min(hi[i], hi[j] - 1)
+    sigs = [signature(c) for c in cmds]
+    classes: Dict[str, List[int]] = {}
+    for i, sg in enumerate(sigs):
+        if sg is not None:
+            classes.setdefault(sg, []).append(i)
+    fixed = [False] * n
+
+    def narrow(starts: List[int]) -> None:
+        work = list(starts)
+        while work:
+            i = work.pop()
+            for j in succs[i]:
+                if lo[j] < lo[i] + 1:
+                    lo[j] = lo[i] + 1
+                    work.append(j)
+        work = list(starts)
+        while work:
+            i = work.pop()
+            for j in preds[i]:
+                if hi[j] > hi[i] - 1:
+                    hi[j] = hi[i] - 1
+                    work.append(j)
+
+    while True:
+        best = (1, None, None)
+        for sg, members in classes.items():
+            ev = []
+            for i in members:
+                if not fixed[i]:
+                    ev.append((lo[i], 0))
+                    ev.append((hi[i], 1))
+            if len(ev) < 4:
+                continue
+            ev.sort()
+            cur = 0
+            for lv, kind in ev:
+                if kind == 0:
+                    cur += 1
+                    if cur > best[0]:
+                        best = (cur, sg, lv)
+                else:
+                    cur -= 1
+        count, sg, lv = best
+        if sg is None:
+            break
+        chosen = [i for i in classes[sg] if not fixed[i] and lo[i] <= lv <= hi[i]]
+        for i in chosen:
+            lo[i] = hi[i] = lv
+            fixed[i] = True
+        narrow(chosen)
+        classes[sg] = [i for i in classes[sg] if not fixed[i]]
+    return lo
+
+
 def _schedule_segment(cmds: List, signature) -> List:
     if len(cmds) < 2:
         return list(cmds)
-    level: List[int] = []
-    last_write: Dict[int, int] = {}        # buffer -> level of its last writer
-    last_read: Dict[int, int] = {}         # buffer -> max level of its readers since that write
-    last_host = -1
-    for c in cmds:
-        r, w = _rw(c)
-        lv = 0
-        for b in r:
-            if b in last_write:
-                lv = max(lv, last_write[b] + 1)
-        for b in w:
-            if b in last_write:
-                lv = max(lv, last_write[b] + 1)
-            if b in last_read:
-                lv = max(lv, last_read[b] + 1)
-        if type(c).__name__ in HOST:
-            lv = max(lv, last_host + 1)
-            last_host = lv
-        level.append(lv)
-        for b in r:
-            last_read[b] = max(last_read.get(b, -1), lv)
-        for b in w:
-            last_write[b] = lv
-            last_read.pop(b, None)
+    level = _levels(cmds, signature)
     out: List = []
     for lv in range(max(level) + 1):
         groups: Dict[str, List] = {}

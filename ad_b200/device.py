@@ -64,7 +64,7 @@ class CudaB200Device:
 
     def __init__(self, device: int = 0, use_graphs: bool = True, gemm: str = "auto",
                  verbose: bool = False, comm=None, rowfuse: bool = True, batch: bool = True,
-                 dp: Optional[tuple] = None, nccl_timeout_s: float = 120.0):
+                 dp: Optional[tuple] = None, nccl_timeout_s: float = 120.0, hsplit: bool = True):
         """``dp = (rank, world, uid)``: data-parallel rank of ``world``; ``uid`` is
         the 128-byte NCCL id from ``ad_b200.dist.nccl_unique_id()`` on rank 0,
         shared with every rank by the caller.  The proc is then this rank's shard
@@ -78,6 +78,7 @@ class CudaB200Device:
             self.rank, self.world = rank, world
         self.rowfuse = rowfuse and os.environ.get("AD_ROWFUSE", "1") != "0"
         self.batch = batch and os.environ.get("AD_BATCH", "1") != "0"
+        self.hsplit = hsplit and os.environ.get("AD_HSPLIT", "1") != "0"
         self._spec_cache: Dict[int, codegen.KernelSpec] = {}
         self.use_graphs = use_graphs and os.environ.get("AD_GRAPH", "1") != "0"
         self.gemm = os.environ.get("AD_GEMM", gemm)
@@ -375,29 +376,7 @@ class CudaB200Device:
     # ------------------------------------------------------------ entry point
     def prepare(self, proc) -> ir.Proc:
         """Init pass: plan + allocate memory, upload contents, build all kernels."""
-        proc = ir.copy_structure(ir.conv_proc(proc))
-        if self.world > 1:
-            from . import dist
-            dist.insert_grad_allreduce(proc)
-        if self.rowfuse:
-            from . import rowfuse
-            rowfuse.fuse_rows(proc)
-        if self.batch:
-            from . import batch
-            sizes: Dict[int, int] = {}
-            for c in ir.iter_cmds(proc):
-                if isinstance(c, ir.AllocEntry) and not c.is_temp:
-                    sizes[c.id] = max(sizes.get(c.id, 0), c.size)
-
-            def signature(c):
-                if type(c).__name__ not in ir.COMPUTE_KINDS:
-                    return None
-                sp = self._single_spec(c, sizes)
-                if sp is None and type(c).__name__ in DOT:
-                    from . import gemm
-                    return gemm.tc_signature(self, c)
-                return None if sp is None else sp.src
-            batch.batch_proc(proc, signature)
+        proc = self.transform(proc)
         self.proc = proc
         self._pinned_ptrs: List[int] = []
         self._setup_memory(proc)
@@ -409,6 +388,58 @@ class CudaB200Device:
         self._pending = []
         self._run_proc(proc, self.init, init=True)
         self._compile_pending()
+        return proc
+
+    @classmethod
+    def offline(cls, gemm: str = "auto", rowfuse: bool = True, batch: bool = True,
+                hsplit: bool = True, sm_count: int = 148, world: int = 1) -> "CudaB200Device":
+        """A device object without a GPU context, for the command-level passes
+        only (``transform``; inspection and CPU tests)."""
+        import types
+        self = cls.__new__(cls)
+        self.ctx = types.SimpleNamespace(sm_count=sm_count)
+        self.gemm, self.rowfuse, self.batch, self.hsplit, self.world = gemm, rowfuse, batch, hsplit, world
+        self._spec_cache = {}
+        return self
+
+    @classmethod
+    def passes_only(cls, proc, **kw) -> ir.Proc:
+        """``transform`` on a copy of ``proc`` without a GPU (see ``offline``)."""
+        return cls.offline(**kw).transform(proc)
+
+    def batch_signature(self, c, sizes: Dict[int, int]) -> Optional[str]:
+        """Commands with equal signatures run as one launch when independent:
+        the generated kernel source (tensor-core dots: split + GEMM sources)."""
+        if type(c).__name__ not in ir.COMPUTE_KINDS:
+            return None
+        sp = self._single_spec(c, sizes)
+        if sp is None and type(c).__name__ in DOT:
+            from . import gemm
+            return gemm.tc_signature(self, c)
+        return None if sp is None else sp.src
+
+    def transform(self, proc) -> ir.Proc:
+        """Command-level passes: a private copy of the proc, then the gradient
+        all-reduce rewrite (data parallel), splitting of horizontally fused
+        elementwise groups, row fusion, and batching."""
+        proc = ir.copy_structure(ir.conv_proc(proc))
+        if self.world > 1:
+            from . import dist
+            dist.insert_grad_allreduce(proc)
+        if self.hsplit:
+            from . import hsplit
+            hsplit.split_groups(proc)
+        if self.rowfuse:
+            from . import rowfuse
+            rowfuse.fuse_rows(proc)
+        if self.batch:
+            from . import batch
+            sizes: Dict[int, int] = {}
+            for c in ir.iter_cmds(proc):
+                if isinstance(c, ir.AllocEntry) and not c.is_temp:
+                    sizes[c.id] = max(sizes.get(c.id, 0), c.size)
+
+            batch.batch_proc(proc, lambda c: self.batch_signature(c, sizes))
         return proc
 
     def execute(self, proc) -> None:

@@ -73,7 +73,8 @@ def setup_scratch(dev, proc: ir.Proc) -> None:
         elif type(c).__name__ in ("DotProdNode", "DPElwFuse"):
             dn, M, N, K = codegen.dot_shape(c)
             if use_tensor_cores(dev, M, N, K):
-                need = max(need, tcgen05.scratch_bytes(M, N, K, dev.ctx.sm_count))
+                need = max(need, tcgen05.scratch_bytes(M, N, K, dev.ctx.sm_count,
+                                                       tcgen05.heavy_epilogue(c, 1, dev.ctx.sm_count)))
     if need:
         base = dev.ctx.malloc(need)
         dev.scratch_allocs.append(base)

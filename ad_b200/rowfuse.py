@@ -521,13 +521,15 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
     row_regs: Dict[int, List[List[str]]] = {}     # full-size buffer -> [chunk][lane] var names
     sc_regs: Dict[int, str] = {}                   # per-row scalar buffer -> var
     decl: List[str] = []
-    for b, kind in sorted(kinds.items()):
+    # register names by position, not buffer id: runs that differ only in their
+    # buffers get identical sources (and batch into one launch)
+    for v, (b, kind) in enumerate(sorted(kinds.items())):
         if kind == "row":
-            row_regs[b] = [[f"r{b}_{k}_{j}" for j in range(VEC)] for k in range(nc)]
-            decl.append("float " + ", ".join(f"r{b}_{k}_{j} = 0.0f" for k in range(nc) for j in range(VEC)) + ";")
+            row_regs[b] = [[f"r{v}_{k}_{j}" for j in range(VEC)] for k in range(nc)]
+            decl.append("float " + ", ".join(f"r{v}_{k}_{j} = 0.0f" for k in range(nc) for j in range(VEC)) + ";")
         else:
-            sc_regs[b] = f"s{b}"
-            decl.append(f"float s{b} = 0.0f;")
+            sc_regs[b] = f"s{v}"
+            decl.append(f"float s{v} = 0.0f;")
 
     defined: Set = set()   # (buffer, chunk) for row buffers, buffer for scalars: value is in registers
     staged_loaded: Set = set()

@@ -54,8 +54,8 @@ def tile_n(N: int) -> int:
     return 256 if N > 128 else (128 if N > 64 else 64)
 
 
-def scratch_bytes(M: int, N: int, K: int, sm_count: int = 148) -> int:
-    return _layout_bytes(M, N, K, 1, 1, 1, sm_count)
+def scratch_bytes(M: int, N: int, K: int, sm_count: int = 148, raw: bool = False) -> int:
+    return _layout_bytes(M, N, K, 1, 1, 1, sm_count, raw)
 
 
 def _ksplit_for(M: int, N: int, K: int, n_inst: int, sm_count: int) -> int:
@@ -64,13 +64,14 @@ def _ksplit_for(M: int, N: int, K: int, n_inst: int, sm_count: int) -> int:
     return choose_ksplit(units, pad(K, BK) // BKF, sm_count)
 
 
-def _layout_bytes(M: int, N: int, K: int, nA: int, nB: int, n_inst: int, sm_count: int) -> int:
+def _layout_bytes(M: int, N: int, K: int, nA: int, nB: int, n_inst: int, sm_count: int,
+                  raw: bool = False) -> int:
     """Scratch of one (grouped) dot: stacked hi/lo operands, then the split-K
     partial sums."""
     bn = tile_n(N)
     Mp, Np, Kp = pad(M, BM), pad(N, bn), pad(K, BK)
     ks = _ksplit_for(M, N, K, n_inst, sm_count)
-    ws = 4 * n_inst * ks * M * N if ks > 1 else 0
+    ws = 4 * n_inst * ks * M * N if (ks > 1 or raw) else 0
     return 2 * 4 * (nA * Mp * Kp + nB * Np * Kp) + ws + 4096
 
 
@@ -419,33 +420,35 @@ def choose_ksplit(units: int, kblocks: int, sm_count: int) -> int:
 
 
 def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int, sm_count: int = 148,
-             n_inst: int = 1, ksplit: int = 1) -> KernelSpec:
+             n_inst: int = 1, ksplit: int = 1, raw_out: bool = False) -> KernelSpec:
     """The GEMM kernel of dot command ``c``.  With ``n_inst > 1`` it is a grouped
     launch over ``n_inst`` commands whose kernels differ only in their pointers:
     the kernel then takes a device table, per instance ``[A row base, B row base,
     epilogue pointers...]`` (row bases index the stacked split operands).
     With ``ksplit > 1`` each output tile is computed as ``ksplit`` partial sums
     over consecutive K ranges, stored raw to ``ad_ws[inst][slice][M][N]``; the
-    fused epilogue then runs in ``gen_splitk_epilogue``'s kernel."""
+    fused epilogue then runs in ``gen_splitk_epilogue``'s kernel; ``raw_out``
+    does the same with one slice (epilogues too heavy for the GEMM's warps)."""
     rng = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
     it = index_type(_epi_only(c), rng)
     bufs, em = codegen.make_emitter(c, it)
     tabw = 2 + len(bufs)
-    if ksplit == 1:
+    raw = ksplit > 1 or raw_out
+    if not raw:
         epi = dot_epilogue(c, em, it, "accv", {"X": "om", "Y": "on", "G": f"(om * ({it}){N} + on)"})
         epi = "\n                    ".join(epi.split("\n"))
     else:
         epi = (f"ad_ws[((long long)(inst * {ksplit} + ks) * {M} + (long long)om) * {N} + (long long)on] = accv;")
     if n_inst == 1:
-        params = ("".join(f"float* __restrict__ p{i}, " for i in range(len(bufs))) if ksplit == 1
+        params = ("".join(f"float* __restrict__ p{i}, " for i in range(len(bufs))) if not raw
                   else "float* __restrict__ ad_ws, ")
         a_row, b_row, epi_ptrs = "0", "0", ""
     else:
         params = "const unsigned long long* __restrict__ ad_tab, " + \
-            ("float* __restrict__ ad_ws, " if ksplit > 1 else "")
+            ("float* __restrict__ ad_ws, " if raw else "")
         a_row = f"(int)ad_tab[(unsigned)inst * {tabw}u]"
         b_row = f"(int)ad_tab[(unsigned)inst * {tabw}u + 1u]"
-        epi_ptrs = "" if ksplit > 1 else "\n            ".join(
+        epi_ptrs = "" if raw else "\n            ".join(
             f"float* __restrict__ p{i} = reinterpret_cast<float*>(ad_tab[(unsigned)inst * {tabw}u + {2 + i}u]);"
             for i in range(len(bufs)))
     kb = pad(K, BK) // BKF
@@ -462,7 +465,7 @@ def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int, sm_coun
     grid = (min(n_inst * mblk * nblk * ksplit, sm_count), 1, 1)
     rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
     epi_bytes = codegen.written_reads_bytes(_epi_only(c), rngw, {})
-    if ksplit > 1:
+    if raw:
         bufs = []
         epi_bytes = 4 * ksplit * M * N
     spec = KernelSpec(name, src, bufs, grid, (320, 1, 1), smem, "gemm_tcgen05",
@@ -551,7 +554,22 @@ def _operands(cmds, name: str):
 
 def group_scratch_bytes(cmds, sm_count: int = 148) -> int:
     (sa, sb), (M, N, K, bn, Mp, Np, Kp) = _operands(cmds, "k")
-    return _layout_bytes(M, N, K, len(sa[0]), len(sb[0]), len(cmds), sm_count)
+    return _layout_bytes(M, N, K, len(sa[0]), len(sb[0]), len(cmds), sm_count,
+                         heavy_epilogue(cmds[0], len(cmds), sm_count))
+
+
+def heavy_epilogue(c, n_inst: int, sm_count: int) -> bool:
+    """Run the fused epilogue as its own kernel when it reads much more than the
+    product itself (more than 4 extra floats per output: e.g. the sum of every
+    head's input gradient fused into one head's dot) and the GEMM's tiles would
+    leave SMs idle: the GEMM's epilogue warps on a few SMs cannot pull that
+    traffic, a kernel over the whole GPU can."""
+    dn, M, N, K = dot_shape(c)
+    bn = tile_n(N)
+    tiles = n_inst * (pad(M, BM) // BM) * (pad(N, bn) // bn)
+    rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
+    epi_bytes = codegen.written_reads_bytes(_epi_only(c), rngw, {})
+    return tiles < 2 * sm_count and epi_bytes > 4 * 6 * M * N
 
 
 def _split_launch(specs, name: str, hi: int, lo: int, stride: int) -> KernelSpec:
@@ -588,13 +606,14 @@ def plan_group(dev, cmds, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
     n = len(cmds)
     sm = dev.ctx.sm_count
     ks = _ksplit_for(M, N, K, n, sm)
+    raw = ks > 1 or heavy_epilogue(cmds[0], n, sm)
     ws = b_lo + 4 * nB * Np * Kp
-    g = gen_gemm(cmds[0], name + ("_tc" if n == 1 else "_tcx"), M, N, K, bn, stages, sm, n, ks)
+    g = gen_gemm(cmds[0], name + ("_tc" if n == 1 else "_tcx"), M, N, K, bn, stages, sm, n, ks, raw)
     sw = BKF * 4
     maps = [rt.tmap_2d(a_hi, nA * Mp, Kp, 4 * Kp, 128, BKF, 4, sw), rt.tmap_2d(a_lo, nA * Mp, Kp, 4 * Kp, 128, BKF, 4, sw),
             rt.tmap_2d(b_hi, nB * Np, Kp, 4 * Kp, bn, BKF, 4, sw), rt.tmap_2d(b_lo, nB * Np, Kp, 4 * Kp, bn, BKF, 4, sw)]
     g.extra["prefix"] = [ctypes.create_string_buffer(m, 128) for m in maps]
-    g.extra["suffix"] = ([ctypes.c_uint64(ws)] if ks > 1 else []) + [ctypes.c_uint64(dev.err_ptr)]
+    g.extra["suffix"] = ([ctypes.c_uint64(ws)] if raw else []) + [ctypes.c_uint64(dev.err_ptr)]
     specs = [split_a, split_b, g]
     rows = []
     if n > 1:
@@ -604,7 +623,7 @@ def plan_group(dev, cmds, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
         g.buffers = []
         g.extra["table"] = rows
         g.extra["nparam"] = g.extra["tabw"]
-    if ks > 1:
+    if raw:
         e = gen_splitk_epilogue(cmds[0], name + ("_ske" if n == 1 else "_skex"), M, N, ks, n)
         e.extra["suffix"] = [ctypes.c_uint64(ws)]
         if n > 1:
