@@ -203,9 +203,58 @@ class Emitter:
             if k.is_temp:
                 return temps[k.id]
             return self.at(k, env)
+        flat = concat_pieces(k)
+        if flat is not None:
+            var, pieces, ths = flat
+            v = self.expr(var, env)
+
+            def search(lo: int, hi: int) -> str:
+                # pieces[lo:hi]; piece i is selected when var > ths[i] (ths[0] = -inf)
+                if hi - lo == 1:
+                    return self.scalar_karg(pieces[lo], env, temps)
+                mid = (lo + hi) // 2
+                return f"(({v}) > {ths[mid]} ? ({search(mid, hi)}) : ({search(lo, mid)}))"
+            return search(0, len(pieces))
         c = self.expr(k.condition, env)
         return (f"({c} ? ({self.scalar_karg(k.karg_two, env, temps)}) : "
                 f"({self.scalar_karg(k.karg_one, env, temps)}))")
+
+
+def _gt_const(cond):
+    if isinstance(cond, ir.Bin) and cond.op == "MoreThan" and isinstance(cond.b, ir.Const):
+        return cond.a, cond.b.val
+    return None
+
+
+def concat_pieces(k):
+    """A tree of ``KConcat`` whose conditions all read ``v > c`` for one
+    expression ``v`` (the reference's nested concatenations along one axis,
+    opencl/karg.py:52) as its in-order pieces and thresholds: piece i is the
+    value where ``ths[i] < v <= ths[i + 1]``.  None unless there are at least
+    4 pieces with strictly increasing thresholds.  Selecting by binary search
+    over the thresholds picks the same piece as the nested conditionals."""
+    gc = _gt_const(k.condition)
+    if gc is None:
+        return None
+    var = gc[0]
+    pieces, ths = [], [None]
+
+    def walk(n) -> bool:
+        if isinstance(n, ir.KConcat):
+            g = _gt_const(n.condition)
+            if g is not None and g[0] == var:
+                if not walk(n.karg_one):
+                    return False
+                ths.append(g[1])
+                return walk(n.karg_two)
+        pieces.append(n)
+        return True
+
+    if not walk(k) or len(pieces) < 4:
+        return None
+    if any(b <= a for a, b in zip(ths[1:], ths[2:])):
+        return None
+    return var, pieces, ths
 
 
 def cmd_written(c) -> set:
