@@ -225,15 +225,22 @@ def batched_source(src: str, name: str) -> Tuple[str, int]:
     if m is None:
         raise ValueError("kernel signature not found")
     params = [x.strip() for x in m.group(3).split(",") if x.strip()]
+    body = src[m.end():]
     decls = []
     for i, prm in enumerate(params):
         typ, pname = prm.rsplit(" ", 1)
         if "*" not in typ:
             raise ValueError(f"non-pointer parameter {prm}")
         base = typ.replace("__restrict__", "").strip()
-        decls.append(f"    {typ} {pname} = reinterpret_cast<{base}>("
-                     f"ad_tab[(unsigned long long)blockIdx.z * {len(params)} + {i}]);")
+        slot = f"ad_tab[(unsigned long long)blockIdx.z * {len(params)} + {i}]"
+        uses = re.findall(rf"\b{pname}\b(.)", body)
+        if len(params) > 16 and uses and all(u == "[" for u in uses):
+            # many pointers (a concatenation's pieces): read each from the table
+            # where it is indexed, so only the pieces actually selected are loaded
+            body = re.sub(rf"\b{pname}\[", f"(reinterpret_cast<{base}>({slot}))[", body)
+            continue
+        decls.append(f"    {typ} {pname} = reinterpret_cast<{base}>({slot});")
     lb = m.group(1) or ""
     head = (f'extern "C" __global__ void {lb}{name}(const unsigned long long* __restrict__ ad_tab) {{\n'
             + "\n".join(decls) + "\n")
-    return src[:m.start()] + head + src[m.end():], len(params)
+    return src[:m.start()] + head + body, len(params)

@@ -184,7 +184,7 @@ class CudaB200Device:
             bufs, err = entry[0], entry[1]
             pre, post = (entry[2], entry[3]) if len(entry) > 2 else ([], [])
             row = list(pre) + [self.view_ptr(v) for v in bufs] + ([self.err_ptr] if err else []) + list(post)
-            assert len(row) == spec.extra["nparam"]
+            assert spec.extra["nparam"] is None or len(row) == spec.extra["nparam"]
             rows += row
         a = np.asarray(rows, dtype=np.uint64)
         p = self.ctx.malloc(a.nbytes)

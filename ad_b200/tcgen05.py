@@ -26,6 +26,7 @@ No TMA multicast is used anywhere.
 from __future__ import annotations
 
 import ctypes
+import re
 from typing import Dict, List
 
 from . import codegen, exprs, ir
@@ -90,11 +91,14 @@ def gen_split(karg: ir.KernelArg, name: str, rows: int, kdim: int, rows_p: int, 
     if rows_p * k_p >= (1 << 31) - 64:
         it = "long long"
     em = Emitter(bufs, it)
+    # read along whichever axis the data is contiguous in (for a concatenation:
+    # the axis all of its pieces are contiguous in)
     orient = "k"
-    if isinstance(karg, ir.KMatrix) and not karg.is_temp:
-        if exprs.lanes(karg.access, k_var, 4).s == 1:
+    leaves = codegen._kmats_of(karg)
+    if leaves and len(leaves) == len(_leaves(karg)):
+        if all(exprs.lanes(km.access, k_var, 4).s == 1 for km in leaves):
             orient = "k"
-        elif exprs.lanes(karg.access, row_var, 4).s == 1:
+        elif all(exprs.lanes(km.access, row_var, 4).s == 1 for km in leaves):
             orient = "r"
     env = {row_var: "gr", k_var: "gk", "G": f"(({it})0)"}
     val = em.scalar_karg(karg, env, {})
@@ -129,6 +133,12 @@ def gen_split(karg: ir.KernelArg, name: str, rows: int, kdim: int, rows_p: int, 
 """
     return KernelSpec(name, src, bufs, (k_p // 32, rows_p // 32, 1), (32, 8, 1), 0, "split",
                       4 * rows * kdim + 8 * rows_p * k_p)
+
+
+def _leaves(k):
+    if isinstance(k, ir.KConcat):
+        return _leaves(k.karg_one) + _leaves(k.karg_two)
+    return [k]
 
 
 def _karg_exprs(k):
@@ -572,20 +582,55 @@ def heavy_epilogue(c, n_inst: int, sm_count: int) -> bool:
     return tiles < 2 * sm_count and epi_bytes > 4 * 6 * M * N
 
 
-def _split_launch(specs, name: str, hi: int, lo: int, stride: int) -> KernelSpec:
-    """One launch splitting every distinct operand: operand u goes to rows
-    ``[u * rows_p, (u + 1) * rows_p)`` of the stacked hi/lo arrays."""
-    if len(specs) == 1:
-        sp = specs[0]
-        sp.extra["suffix"] = [ctypes.c_uint64(hi), ctypes.c_uint64(lo)]
-        return sp
-    from .batch import batched_source
-    first = specs[0]
-    src, nparam = batched_source(first.src, name)
-    sp = KernelSpec(name, src, [], (first.grid[0], first.grid[1], len(specs)), first.block, first.smem,
-                    "split_batched", sum(x.bytes_moved for x in specs))
-    sp.extra["table"] = [(x.buffers, False, [], [hi + u * stride, lo + u * stride]) for u, x in enumerate(specs)]
-    sp.extra["nparam"] = nparam
+_KSIG = re.compile(r'extern "C" __global__ void __launch_bounds__\(256\) (\w+)\(([^)]*)\)\s*\{')
+
+
+def _split_pair(sa, sb, name: str, a_hi: int, a_lo: int, a_stride: int,
+                b_hi: int, b_lo: int, b_stride: int) -> KernelSpec:
+    """One launch splitting every distinct A operand and every distinct B
+    operand.  A flat grid enumerates each operand's 32 x 32 tiles (A's
+    operands first); pointers come from a device table (per operand: its
+    views, then its hi and lo destinations).  Operand u of A goes to rows
+    ``[u * rows_p, (u + 1) * rows_p)`` of the stacked hi/lo arrays, likewise B."""
+    parts, calls, rows = [], [], []
+    cbase, tbase = 0, 0
+    for tag, specs, hi, lo, stride in (("a", sa, a_hi, a_lo, a_stride), ("b", sb, b_hi, b_lo, b_stride)):
+        first = specs[0]
+        m = _KSIG.search(first.src)
+        fn = f"{name}_{tag}"
+        width = len(first.buffers) + 2
+        # pointers are read from the table where they are used: a concatenated
+        # operand has one per piece, and only the selected piece's is needed
+        body = first.src[m.end():].replace("blockIdx.x", "ad_bx").replace("blockIdx.y", "ad_by")
+        body = re.sub(r"\bp(\d+)\[", r"((const float*)ad_t[\1])[", body)
+        body = body.replace("hi[", f"((float*)ad_t[{width - 2}])[").replace("lo[", f"((float*)ad_t[{width - 1}])[")
+        parts.append(first.src[:m.start()] + f"__device__ __forceinline__ void {fn}("
+                     f"const unsigned long long* __restrict__ ad_t, unsigned ad_bx, unsigned ad_by) {{" + body)
+        args = "t"
+        n = len(specs)
+        gx, gy = first.grid[0], first.grid[1]
+        per = gx * gy
+        calls.append(f"""    if (c < {cbase + n * per}u) {{
+        const unsigned r = c - {cbase}u, u = r / {per}u, w = r - u * {per}u;
+        const unsigned long long* t = tab + {tbase} + (unsigned long long)u * {width};
+        {fn}({args}, w % {gx}u, w / {gx}u);
+        return;
+    }}""")
+        for u, x in enumerate(specs):
+            rows.append((x.buffers, False, [], [hi + u * stride, lo + u * stride]))
+        cbase += n * per
+        tbase += n * width
+    src = "\n".join(parts) + f"""
+extern "C" __global__ void __launch_bounds__(256) {name}(const unsigned long long* __restrict__ tab) {{
+    const unsigned c = blockIdx.x;
+{chr(10).join(calls)}
+}}
+"""
+    assert sa[0].block == sb[0].block == (32, 8, 1)
+    sp = KernelSpec(name, src, [], (cbase, 1, 1), sa[0].block, 0, "split",
+                    sum(x.bytes_moved for x in sa) + sum(x.bytes_moved for x in sb))
+    sp.extra["table"] = rows
+    sp.extra["nparam"] = None
     return sp
 
 
@@ -601,8 +646,7 @@ def plan_group(dev, cmds, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
     a_hi, a_lo = base, base + 4 * nA * Mp * Kp
     b_hi = a_lo + 4 * nA * Mp * Kp
     b_lo = b_hi + 4 * nB * Np * Kp
-    split_a = _split_launch(sa, name + "_splitA_x", a_hi, a_lo, 4 * Mp * Kp)
-    split_b = _split_launch(sb, name + "_splitB_x", b_hi, b_lo, 4 * Np * Kp)
+    split = _split_pair(sa, sb, name + "_split", a_hi, a_lo, 4 * Mp * Kp, b_hi, b_lo, 4 * Np * Kp)
     n = len(cmds)
     sm = dev.ctx.sm_count
     ks = _ksplit_for(M, N, K, n, sm)
@@ -614,7 +658,7 @@ def plan_group(dev, cmds, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
             rt.tmap_2d(b_hi, nB * Np, Kp, 4 * Kp, bn, BKF, 4, sw), rt.tmap_2d(b_lo, nB * Np, Kp, 4 * Kp, bn, BKF, 4, sw)]
     g.extra["prefix"] = [ctypes.create_string_buffer(m, 128) for m in maps]
     g.extra["suffix"] = ([ctypes.c_uint64(ws)] if raw else []) + [ctypes.c_uint64(dev.err_ptr)]
-    specs = [split_a, split_b, g]
+    specs = [split, g]
     rows = []
     if n > 1:
         for i, c in enumerate(cmds):

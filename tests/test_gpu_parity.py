@@ -128,8 +128,8 @@ def test_batching_groups_attention_blocks():
 
 def test_grouped_tensor_core_dots():
     """Same-kernel dot commands of one dependency level become one grouped
-    tcgen05 launch; operands read by every member (the layer input of the
-    per-head projections) are split once."""
+    tcgen05 launch after one split launch for all their operands; operands read
+    by every member (the layer input of the per-head projections) are split once."""
     from ad_b200.device import CudaB200Device
     p, _ = load_case("enc_1_8_128_512_8_2048_100")
     d = CudaB200Device(gemm="tc")
@@ -140,10 +140,10 @@ def test_grouped_tensor_core_dots():
         if "gemm_tcgen05" in kinds:
             g = ls[kinds.index("gemm_tcgen05")].spec
             if "table" in g.extra:
-                groups[len(g.extra["table"])] = (kinds[0], kinds[1])
+                groups[len(g.extra["table"])] = len(ls[0].spec.extra["table"])   # operands split
     d.close()
     assert max(groups) == 64
-    assert groups[24] == ("split", "split_batched")
+    assert groups[24] == 1 + 24          # the shared input once, each head's weight
 
 
 @pytest.mark.parametrize("shape,n", [((512, 64, 4096), 1), ((512, 64, 4096), 6), ((640, 200, 3000), 3)])
