@@ -62,6 +62,7 @@ typedef CUresult (*PFN_ModuleUnload)(CUmodule);
 typedef CUresult (*PFN_ModuleGetFunction)(CUfunction*, CUmodule, const char*);
 typedef CUresult (*PFN_LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned,
                                       unsigned, unsigned, CUstream, void**, void**);
+typedef CUresult (*PFN_LaunchKernelEx)(const CUlaunchConfig*, CUfunction, void**, void**);
 typedef CUresult (*PFN_FuncSetAttribute)(CUfunction, CUfunction_attribute, int);
 typedef CUresult (*PFN_FuncGetAttribute)(int*, CUfunction_attribute, CUfunction);
 typedef CUresult (*PFN_GetErrorString)(CUresult, const char**);
@@ -77,6 +78,7 @@ struct Driver {
   PFN_ModuleUnload moduleUnload = nullptr;
   PFN_ModuleGetFunction moduleGetFunction = nullptr;
   PFN_LaunchKernel launchKernel = nullptr;
+  PFN_LaunchKernelEx launchKernelEx = nullptr;
   PFN_FuncSetAttribute funcSetAttribute = nullptr;
   PFN_FuncGetAttribute funcGetAttribute = nullptr;
   PFN_GetErrorString getErrorString = nullptr;
@@ -103,6 +105,7 @@ int driver() {
   if (get_entry("cuModuleUnload", &g_drv.moduleUnload)) return 1;
   if (get_entry("cuModuleGetFunction", &g_drv.moduleGetFunction)) return 1;
   if (get_entry("cuLaunchKernel", &g_drv.launchKernel)) return 1;
+  if (get_entry("cuLaunchKernelEx", &g_drv.launchKernelEx)) return 1;
   if (get_entry("cuFuncSetAttribute", &g_drv.funcSetAttribute)) return 1;
   if (get_entry("cuFuncGetAttribute", &g_drv.funcGetAttribute)) return 1;
   if (get_entry("cuGetErrorString", &g_drv.getErrorString)) return 1;
@@ -478,6 +481,37 @@ int ad_launch(ad_ctx* c, ad_kernel* k, unsigned gx, unsigned gy, unsigned gz, un
   if (r != CUDA_SUCCESS) {
     char what[256];
     snprintf(what, sizeof(what), "cuLaunchKernel(%s grid=%u,%u,%u block=%u,%u,%u smem=%u)",
+             k->name.c_str(), gx, gy, gz, bx, by, bz, smem);
+    return cu_fail(r, what);
+  }
+  return 0;
+}
+
+int ad_launch_pdl(ad_ctx* c, ad_kernel* k, unsigned gx, unsigned gy, unsigned gz, unsigned bx,
+                  unsigned by, unsigned bz, unsigned smem, void** args, int stream) {
+  cudaStream_t s;
+  if (stream_of(c, stream, &s)) return 1;
+  if (!k) return fail("null kernel");
+  CUlaunchAttribute attr[1];
+  memset(attr, 0, sizeof(attr));
+  attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+  attr[0].value.programmaticStreamSerializationAllowed = 1;
+  CUlaunchConfig cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDimX = gx;
+  cfg.gridDimY = gy;
+  cfg.gridDimZ = gz;
+  cfg.blockDimX = bx;
+  cfg.blockDimY = by;
+  cfg.blockDimZ = bz;
+  cfg.sharedMemBytes = smem;
+  cfg.hStream = (CUstream)s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CUresult r = g_drv.launchKernelEx(&cfg, k->fn, args, nullptr);
+  if (r != CUDA_SUCCESS) {
+    char what[256];
+    snprintf(what, sizeof(what), "cuLaunchKernelEx(%s grid=%u,%u,%u block=%u,%u,%u smem=%u, PDL)",
              k->name.c_str(), gx, gy, gz, bx, by, bz, smem);
     return cu_fail(r, what);
   }

@@ -45,9 +45,9 @@ def tc_signature(dev, cmd) -> str:
     from . import tcgen05
     dn, M, N, K = codegen.dot_shape(cmd)
     bn = tcgen05.tile_n(N)
-    (sa, sb), _ = tcgen05._operands([cmd], "k")
+    gp = tcgen05.GroupPlan([cmd])
     g = tcgen05.gen_gemm(cmd, "k", M, N, K, bn, tcgen05.stages_for(bn))
-    return "\n".join(["tc", sa[0][0].src, sb[0][0].src, g.src])
+    return "\n".join(["tc", gp.sa[0].src, gp.sb[0].src, g.src])
 
 
 def plan_dot(dev, cmd, name: str, sizes: Dict[int, int]) -> List[codegen.KernelSpec]:
@@ -73,8 +73,7 @@ def setup_scratch(dev, proc: ir.Proc) -> None:
         elif type(c).__name__ in ("DotProdNode", "DPElwFuse"):
             dn, M, N, K = codegen.dot_shape(c)
             if use_tensor_cores(dev, M, N, K):
-                need = max(need, tcgen05.scratch_bytes(M, N, K, dev.ctx.sm_count,
-                                                       tcgen05.heavy_epilogue(c, 1, dev.ctx.sm_count)))
+                need = max(need, tcgen05.group_scratch_bytes([c], dev.ctx.sm_count))
     if need:
         base = dev.ctx.malloc(need)
         dev.scratch_allocs.append(base)

@@ -55,27 +55,6 @@ def tile_n(N: int) -> int:
     return 256 if N > 128 else (128 if N > 64 else 64)
 
 
-def scratch_bytes(M: int, N: int, K: int, sm_count: int = 148, raw: bool = False) -> int:
-    return _layout_bytes(M, N, K, 1, 1, 1, sm_count, raw)
-
-
-def _ksplit_for(M: int, N: int, K: int, n_inst: int, sm_count: int) -> int:
-    bn = tile_n(N)
-    units = n_inst * (pad(M, BM) // BM) * (pad(N, bn) // bn)
-    return choose_ksplit(units, pad(K, BK) // BKF, sm_count)
-
-
-def _layout_bytes(M: int, N: int, K: int, nA: int, nB: int, n_inst: int, sm_count: int,
-                  raw: bool = False) -> int:
-    """Scratch of one (grouped) dot: stacked hi/lo operands, then the split-K
-    partial sums."""
-    bn = tile_n(N)
-    Mp, Np, Kp = pad(M, BM), pad(N, bn), pad(K, BK)
-    ks = _ksplit_for(M, N, K, n_inst, sm_count)
-    ws = 4 * n_inst * ks * M * N if (ks > 1 or raw) else 0
-    return 2 * 4 * (nA * Mp * Kp + nB * Np * Kp) + ws + 4096
-
-
 # ---------------------------------------------------------------- split kernel
 
 def gen_split(karg: ir.KernelArg, name: str, rows: int, kdim: int, rows_p: int, k_p: int,
@@ -208,10 +187,10 @@ __device__ __forceinline__ void mma_tf32(unsigned tmem, unsigned long long ad, u
 __device__ __forceinline__ void mma_commit(unsigned long long* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ void tile_of(int t, int& m_blk, int& n_blk) {
+__device__ __forceinline__ void tile_of_n(int t, int num_n, int& m_blk, int& n_blk) {
     // grouped raster: GROUP m-blocks share each sweep over n so A panels stay in L2
-    constexpr int GROUP = GROUP_M, NUM_M = M_BLOCKS, NUM_N = N_BLOCKS;
-    const int per_group = GROUP * NUM_N;
+    constexpr int GROUP = GROUP_M, NUM_M = M_BLOCKS;
+    const int per_group = GROUP * num_n;
     const int g = t / per_group, first = g * GROUP;
     const int gsz = (NUM_M - first) < GROUP ? (NUM_M - first) : GROUP;
     const int r = t % per_group;
@@ -219,16 +198,7 @@ __device__ __forceinline__ void tile_of(int t, int& m_blk, int& n_blk) {
     n_blk = r / gsz;
 }
 
-__device__ __forceinline__ void decode(int t, int& inst, int& ks, int& m_blk, int& n_blk) {
-    // instances of a grouped launch are consecutive ranges of KSPLIT x M_BLOCKS x N_BLOCKS
-    // work units; ks = which slice of the K blocks this unit accumulates
-    constexpr int PER = M_BLOCKS * N_BLOCKS;
-    inst = t / (PER * KSPLIT);
-    const int r = t - inst * (PER * KSPLIT);
-    ks = r / PER;
-    tile_of(r - ks * PER, m_blk, n_blk);
-}
-
+DECODE_FN
 // Persistent, warp-specialised: warp 0 = TMA producer, warp 1 = MMA issuer,
 // warps 2..9 = epilogue (TMEM lane quarter = warp % 4, column half = (warp - 2) / 4).
 // Two TMEM accumulators (2 x BN columns) let the epilogue of one tile overlap the
@@ -238,7 +208,7 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
     const __grid_constant__ TmapT tBh, const __grid_constant__ TmapT tBl,
     PARAMS int* __restrict__ err)
 {
-    constexpr int BN = TILE_N, STAGES = NSTAGES, KB = KBLOCKS, NUM_TILES = NUM_INST * M_BLOCKS * N_BLOCKS * KSPLIT;
+    constexpr int BN = TILE_N, STAGES = NSTAGES, KB = KBLOCKS, NUM_TILES = TOTAL_UNITS;
     constexpr unsigned A_BYTES = 128 * ROWB, B_BYTES = BN * ROWB;
     constexpr unsigned STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     constexpr int EPI_WARPS = 8;
@@ -392,11 +362,12 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
                 __syncwarp();
                 // all 32 rows unrolled: the epilogue's global loads (bias, residuals,
                 // in-place parameters) are issued together instead of 4 at a time
+                CHUNK_SETUP
                 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const IDX om = (IDX)m0 + q * 32 + i;
-                    const IDX on = (IDX)n0 + c * 32 + lane;
-                    if (om < (IDX)M_DIM && on < (IDX)N_DIM) {
+                    const IDX on = ON_BASE + lane;
+                    if (CHUNK_OK && om < (IDX)M_DIM && on < (IDX)N_DIM) {
                         const float accv = tr[i * 32 + (lane ^ i)];
                         EPILOGUE
                     }
@@ -429,12 +400,48 @@ def choose_ksplit(units: int, kblocks: int, sm_count: int) -> int:
     return best
 
 
+DECODE_PLAIN = """__device__ __forceinline__ void decode(int t, int& inst, int& ks, int& m_blk, int& n_blk) {
+    // instances of a grouped launch are consecutive ranges of KSPLIT x M_BLOCKS x N_BLOCKS
+    // work units; ks = which slice of the K blocks this unit accumulates
+    constexpr int PER = M_BLOCKS * N_BLOCKS;
+    inst = t / (PER * KSPLIT);
+    const int r = t - inst * (PER * KSPLIT);
+    ks = r / PER;
+    tile_of_n(r - ks * PER, N_BLOCKS, m_blk, n_blk);
+}
+"""
+
+DECODE_SEG = """// segments: instances sharing one A operand whose B operands are consecutive rows
+// of the stacked B, computed as one product over their concatenated columns
+__constant__ int ad_seg_start[NSEG + 1] = {SEG_START};   // first work unit
+__constant__ int ad_seg_nb[NSEG] = {SEG_NB};             // n-blocks
+__constant__ int ad_seg_arow[NSEG] = {SEG_AROW};         // first row in the stacked A
+__constant__ int ad_seg_brow[NSEG] = {SEG_BROW};         // first row in the stacked B
+__constant__ int ad_seg_ncols[NSEG] = {SEG_NCOLS};       // instances x padded N
+__constant__ int ad_seg_first[NSEG] = {SEG_FIRST};       // first instance (table row)
+__device__ __forceinline__ void decode(int t, int& seg, int& ks, int& m_blk, int& n_blk) {
+    int s = 0;
+    while (s + 1 < NSEG && t >= ad_seg_start[s + 1]) ++s;
+    const int r = t - ad_seg_start[s], per = M_BLOCKS * ad_seg_nb[s];
+    seg = s;
+    ks = r / per;
+    tile_of_n(r - ks * per, ad_seg_nb[s], m_blk, n_blk);
+}
+"""
+
+
 def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int, sm_count: int = 148,
-             n_inst: int = 1, ksplit: int = 1, raw_out: bool = False) -> KernelSpec:
+             n_inst: int = 1, ksplit: int = 1, raw_out: bool = False, segments=None,
+             np_stride: int = 0) -> KernelSpec:
     """The GEMM kernel of dot command ``c``.  With ``n_inst > 1`` it is a grouped
     launch over ``n_inst`` commands whose kernels differ only in their pointers:
     the kernel then takes a device table, per instance ``[A row base, B row base,
     epilogue pointers...]`` (row bases index the stacked split operands).
+    With ``segments`` (list of ``(A row base, first instance, count)``), each
+    segment's instances share A and own consecutive ``np_stride``-row blocks
+    of the stacked B: the segment is one product over ``count * np_stride``
+    columns with ``bn``-wide tiles, and every 32-column chunk of the epilogue
+    finds its instance (N fusion of narrow per-head products).
     With ``ksplit > 1`` each output tile is computed as ``ksplit`` partial sums
     over consecutive K ranges, stored raw to ``ad_ws[inst][slice][M][N]``; the
     fused epilogue then runs in ``gen_splitk_epilogue``'s kernel; ``raw_out``
@@ -444,35 +451,65 @@ def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int, sm_coun
     bufs, em = codegen.make_emitter(c, it)
     tabw = 2 + len(bufs)
     raw = ksplit > 1 or raw_out
+    ivar = "cinst" if segments else "inst"
     if not raw:
         epi = dot_epilogue(c, em, it, "accv", {"X": "om", "Y": "on", "G": f"(om * ({it}){N} + on)"})
-        epi = "\n                    ".join(epi.split("\n"))
+        epi = "\n                        ".join(epi.split("\n"))
     else:
-        epi = (f"ad_ws[((long long)(inst * {ksplit} + ks) * {M} + (long long)om) * {N} + (long long)on] = accv;")
-    if n_inst == 1:
-        params = ("".join(f"float* __restrict__ p{i}, " for i in range(len(bufs))) if not raw
-                  else "float* __restrict__ ad_ws, ")
-        a_row, b_row, epi_ptrs = "0", "0", ""
-    else:
-        params = "const unsigned long long* __restrict__ ad_tab, " + \
-            ("float* __restrict__ ad_ws, " if raw else "")
-        a_row = f"(int)ad_tab[(unsigned)inst * {tabw}u]"
-        b_row = f"(int)ad_tab[(unsigned)inst * {tabw}u + 1u]"
-        epi_ptrs = "" if raw else "\n            ".join(
-            f"float* __restrict__ p{i} = reinterpret_cast<float*>(ad_tab[(unsigned)inst * {tabw}u + {2 + i}u]);"
-            for i in range(len(bufs)))
+        epi = (f"ad_ws[((long long)({ivar} * {ksplit} + ks) * {M} + (long long)om) * {N} + (long long)on] = accv;")
+    ptr_decls = lambda iv, ind: f"\n{ind}".join(
+        f"float* __restrict__ p{i} = reinterpret_cast<float*>(ad_tab[(unsigned){iv} * {tabw}u + {2 + i}u]);"
+        for i in range(len(bufs)))
     kb = pad(K, BK) // BKF
-    mblk, nblk = pad(M, BM) // BM, pad(N, bn) // bn
-    src = (GEMM_TEMPLATE.replace("NAME", name).replace("PARAMS", params).replace("TILE_N", str(bn))
+    mblk = pad(M, BM) // BM
+    chunk_setup, on_base, chunk_ok = "", "(IDX)n0 + c * 32", "true"
+    if segments:
+        assert np_stride % 32 == 0 and n_inst > 1
+        params = "const unsigned long long* __restrict__ ad_tab, " + ("float* __restrict__ ad_ws, " if raw else "")
+        nbs = [-(-(cnt * np_stride) // bn) for _, _, cnt in segments]
+        starts = [0]
+        for nb_ in nbs:
+            starts.append(starts[-1] + mblk * nb_ * ksplit)
+        decode = (DECODE_SEG.replace("NSEG", str(len(segments)))
+                  .replace("SEG_START", ", ".join(map(str, starts))).replace("SEG_NB", ", ".join(map(str, nbs)))
+                  .replace("SEG_AROW", ", ".join(str(a) for a, _, _ in segments))
+                  .replace("SEG_BROW", ", ".join(str(f * np_stride) for _, f, _ in segments))
+                  .replace("SEG_NCOLS", ", ".join(str(cnt * np_stride) for _, _, cnt in segments))
+                  .replace("SEG_FIRST", ", ".join(str(f) for _, f, _ in segments)))
+        total = starts[-1]
+        a_row, b_row, epi_ptrs = "ad_seg_arow[inst]", "ad_seg_brow[inst]", ""
+        ind = "\n                "
+        chunk_setup = (f"const int gcol = n0 + c * 32, cj = gcol / {np_stride};" + ind +
+                       f"const bool chunk_ok = gcol < ad_seg_ncols[inst];" + ind +
+                       f"const int cinst = ad_seg_first[inst] + (chunk_ok ? cj : 0);" +
+                       ("" if raw else ind + ptr_decls("cinst", ind)))
+        on_base, chunk_ok = f"(IDX)(gcol - cj * {np_stride})", "chunk_ok"
+        nblk_plain = 1
+    else:
+        nblk_plain = pad(N, bn) // bn
+        total = n_inst * mblk * nblk_plain * ksplit
+        decode = DECODE_PLAIN
+        if n_inst == 1:
+            params = ("".join(f"float* __restrict__ p{i}, " for i in range(len(bufs))) if not raw
+                      else "float* __restrict__ ad_ws, ")
+            a_row, b_row, epi_ptrs = "0", "0", ""
+        else:
+            params = "const unsigned long long* __restrict__ ad_tab, " + ("float* __restrict__ ad_ws, " if raw else "")
+            a_row = f"(int)ad_tab[(unsigned)inst * {tabw}u]"
+            b_row = f"(int)ad_tab[(unsigned)inst * {tabw}u + 1u]"
+            epi_ptrs = "" if raw else ptr_decls("inst", "\n            ")
+    src = (GEMM_TEMPLATE.replace("DECODE_FN", decode).replace("NAME", name).replace("PARAMS", params)
+           .replace("TILE_N", str(bn))
            .replace("NSTAGES", str(stages)).replace("KBLOCKS", str(kb)).replace("GROUP_M", str(GROUP_M))
            .replace("ROWB", str(BKF * 4)).replace("SWZ", "2" if BKF == 32 else "4").replace("BKF", str(BKF))
-           .replace("NUM_INST", str(n_inst)).replace("KSPLIT", str(ksplit))
+           .replace("TOTAL_UNITS", str(total)).replace("KSPLIT", str(ksplit))
            .replace("A_ROW", a_row).replace("B_ROW", b_row).replace("EPI_PTRS", epi_ptrs)
-           .replace("M_BLOCKS", str(mblk)).replace("N_BLOCKS", str(nblk))
+           .replace("CHUNK_SETUP", chunk_setup).replace("ON_BASE", on_base).replace("CHUNK_OK", chunk_ok)
+           .replace("M_BLOCKS", str(mblk)).replace("N_BLOCKS", str(nblk_plain))
            .replace("IDX", it).replace("M_DIM", str(M)).replace("N_DIM", str(N)).replace("EPILOGUE", epi))
     stage_bytes = 2 * 128 * BKF * 4 + 2 * bn * BKF * 4
     smem = stages * stage_bytes + 8 * 4096 + 1024 + 256
-    grid = (min(n_inst * mblk * nblk * ksplit, sm_count), 1, 1)
+    grid = (min(total, sm_count), 1, 1)
     rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
     epi_bytes = codegen.written_reads_bytes(_epi_only(c), rngw, {})
     if raw:
@@ -540,43 +577,79 @@ def plan(dev, cmd, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
     return plan_group(dev, [cmd], name, sizes)
 
 
-def _operands(cmds, name: str):
-    """Split specs of every command's A and B, and the distinct operands among
-    them: commands reading the same data through the same access (the shared
-    input of per-head projections) share one split."""
-    dn, M, N, K = dot_shape(cmds[0])
-    bn = tile_n(N)
-    Mp, Np, Kp = pad(M, BM), pad(N, bn), pad(K, BK)
-    out = []
-    for which, rows, rows_p, rv, kv in ((0, M, Mp, "X", "Y"), (1, N, Np, "Y", "X")):
+class GroupPlan:
+    """How one dot command, or a group of dot commands with identical kernels,
+    runs on the tensor cores: instance order, distinct operands (commands
+    reading the same data through the same access share one split), N-fused
+    segments, tile width, K slices, and where the epilogue runs."""
+
+    def __init__(self, cmds, sm_count: int = 148, name: str = "k"):
+        dn, M, N, K = dot_shape(cmds[0])
+        self.M, self.N, self.K = M, N, K
+        bn0 = tile_n(N)
+        self.Mp, self.Np, self.Kp = pad(M, BM), pad(N, bn0), pad(K, BK)
+        sa, ia = self._dedupe(cmds, 0, name)
+        # N fusion: narrow products (padded N below the widest tile) whose
+        # instances each own a distinct B and share A with others
+        self.segments = None
+        n = len(cmds)
+        if n > 1 and self.Np < 256:
+            sb_try, ib_try = self._dedupe(cmds, 1, name)
+            if len(sb_try) == n and len(sa) < n:
+                order = sorted(range(n), key=lambda i: (ia[i], i))
+                cmds = [cmds[i] for i in order]
+                sa, ia = self._dedupe(cmds, 0, name)
+                segs = []
+                for i, a in enumerate(ia):
+                    if segs and segs[-1][0] == a:
+                        segs[-1][2] += 1
+                    else:
+                        segs.append([a, i, 1])
+                self.segments = [(a * self.Mp, f, cnt) for a, f, cnt in segs]
+        self.cmds = cmds
+        self.sa, self.ia = sa, ia
+        self.sb, self.ib = self._dedupe(cmds, 1, name)
+        mblk = self.Mp // BM
+        if self.segments:
+            self.bn = tile_n(min(cnt for _, _, cnt in self.segments) * self.Np)
+            units = sum(mblk * -(-(cnt * self.Np) // self.bn) for _, _, cnt in self.segments)
+        else:
+            self.bn = bn0
+            units = n * mblk * (self.Np // bn0)
+        self.ks = choose_ksplit(units, self.Kp // BKF, sm_count)
+        self.raw = self.ks > 1 or heavy_epilogue(cmds[0], units, sm_count)
+
+    def _dedupe(self, cmds, which: int, name: str):
+        rows, rows_p, rv, kv = ((self.M, self.Mp, "X", "Y") if which == 0 else (self.N, self.Np, "Y", "X"))
         specs, index, uniq = [], [], {}
         for c in cmds:
             sp = gen_split(dot_shape(c)[0].kargs[which], name + ("_splitA" if which == 0 else "_splitB"),
-                           rows, K, rows_p, Kp, rv, kv)
+                           rows, self.K, rows_p, self.Kp, rv, kv)
             key = (sp.src, tuple(sp.buffers))
             if key not in uniq:
                 uniq[key] = len(specs)
                 specs.append(sp)
             index.append(uniq[key])
-        out.append((specs, index))
-    return out, (M, N, K, bn, Mp, Np, Kp)
+        return specs, index
+
+    def scratch_bytes(self) -> int:
+        """Stacked hi/lo operands, then the partial sums / raw products."""
+        n = len(self.cmds)
+        ws = 4 * n * self.ks * self.M * self.N if self.raw else 0
+        return 2 * 4 * (len(self.sa) * self.Mp * self.Kp + len(self.sb) * self.Np * self.Kp) + ws + 4096
 
 
 def group_scratch_bytes(cmds, sm_count: int = 148) -> int:
-    (sa, sb), (M, N, K, bn, Mp, Np, Kp) = _operands(cmds, "k")
-    return _layout_bytes(M, N, K, len(sa[0]), len(sb[0]), len(cmds), sm_count,
-                         heavy_epilogue(cmds[0], len(cmds), sm_count))
+    return GroupPlan(cmds, sm_count).scratch_bytes()
 
 
-def heavy_epilogue(c, n_inst: int, sm_count: int) -> bool:
+def heavy_epilogue(c, tiles: int, sm_count: int) -> bool:
     """Run the fused epilogue as its own kernel when it reads much more than the
     product itself (more than 4 extra floats per output: e.g. the sum of every
-    head's input gradient fused into one head's dot) and the GEMM's tiles would
-    leave SMs idle: the GEMM's epilogue warps on a few SMs cannot pull that
-    traffic, a kernel over the whole GPU can."""
+    head's input gradient fused into one head's dot) and the GEMM's ``tiles``
+    would leave SMs idle: the GEMM's epilogue warps on a few SMs cannot pull
+    that traffic, a kernel over the whole GPU can."""
     dn, M, N, K = dot_shape(c)
-    bn = tile_n(N)
-    tiles = n_inst * (pad(M, BM) // BM) * (pad(N, bn) // bn)
     rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
     epi_bytes = codegen.written_reads_bytes(_epi_only(c), rngw, {})
     return tiles < 2 * sm_count and epi_bytes > 4 * 6 * M * N
@@ -639,36 +712,36 @@ def plan_group(dev, cmds, name: str, sizes: Dict[int, int]) -> List[KernelSpec]:
     with identical kernels (same shapes, accesses and epilogue; different
     buffers) as one grouped launch each."""
     from . import runtime as rt
-    ((sa, ia), (sb, ib)), (M, N, K, bn, Mp, Np, Kp) = _operands(cmds, name)
-    stages = stages_for(bn)
-    nA, nB = len(sa), len(sb)
+    sm = dev.ctx.sm_count
+    gp = GroupPlan(cmds, sm, name)
+    cmds = gp.cmds
+    M, N, K, Mp, Np, Kp, bn = gp.M, gp.N, gp.K, gp.Mp, gp.Np, gp.Kp, gp.bn
+    nA, nB, n = len(gp.sa), len(gp.sb), len(cmds)
     base = dev.scratch_base
     a_hi, a_lo = base, base + 4 * nA * Mp * Kp
     b_hi = a_lo + 4 * nA * Mp * Kp
     b_lo = b_hi + 4 * nB * Np * Kp
-    split = _split_pair(sa, sb, name + "_split", a_hi, a_lo, 4 * Mp * Kp, b_hi, b_lo, 4 * Np * Kp)
-    n = len(cmds)
-    sm = dev.ctx.sm_count
-    ks = _ksplit_for(M, N, K, n, sm)
-    raw = ks > 1 or heavy_epilogue(cmds[0], n, sm)
     ws = b_lo + 4 * nB * Np * Kp
-    g = gen_gemm(cmds[0], name + ("_tc" if n == 1 else "_tcx"), M, N, K, bn, stages, sm, n, ks, raw)
+    assert gp.scratch_bytes() <= dev.scratch_bytes
+    split = _split_pair(gp.sa, gp.sb, name + "_split", a_hi, a_lo, 4 * Mp * Kp, b_hi, b_lo, 4 * Np * Kp)
+    g = gen_gemm(cmds[0], name + ("_tc" if n == 1 else "_tcx"), M, N, K, bn, stages_for(bn), sm, n,
+                 gp.ks, gp.raw, gp.segments, Np)
     sw = BKF * 4
     maps = [rt.tmap_2d(a_hi, nA * Mp, Kp, 4 * Kp, 128, BKF, 4, sw), rt.tmap_2d(a_lo, nA * Mp, Kp, 4 * Kp, 128, BKF, 4, sw),
             rt.tmap_2d(b_hi, nB * Np, Kp, 4 * Kp, bn, BKF, 4, sw), rt.tmap_2d(b_lo, nB * Np, Kp, 4 * Kp, bn, BKF, 4, sw)]
     g.extra["prefix"] = [ctypes.create_string_buffer(m, 128) for m in maps]
-    g.extra["suffix"] = ([ctypes.c_uint64(ws)] if raw else []) + [ctypes.c_uint64(dev.err_ptr)]
+    g.extra["suffix"] = ([ctypes.c_uint64(ws)] if gp.raw else []) + [ctypes.c_uint64(dev.err_ptr)]
     specs = [split, g]
     rows = []
     if n > 1:
         for i, c in enumerate(cmds):
             bufs, _ = codegen.make_emitter(c, "int")
-            rows.append((bufs, False, [ia[i] * Mp, ib[i] * Np], []))
+            rows.append((bufs, False, [gp.ia[i] * Mp, gp.ib[i] * Np], []))
         g.buffers = []
         g.extra["table"] = rows
         g.extra["nparam"] = g.extra["tabw"]
-    if raw:
-        e = gen_splitk_epilogue(cmds[0], name + ("_ske" if n == 1 else "_skex"), M, N, ks, n)
+    if gp.raw:
+        e = gen_splitk_epilogue(cmds[0], name + ("_ske" if n == 1 else "_skex"), M, N, gp.ks, n)
         e.extra["suffix"] = [ctypes.c_uint64(ws)]
         if n > 1:
             e.extra["table"] = rows

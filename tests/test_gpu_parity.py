@@ -152,10 +152,30 @@ def test_split_k_dots(shape, n):
     a fused epilogue kernel; single and grouped, ragged shapes included."""
     from ad_b200 import tcgen05
     M, N, K = shape
-    assert tcgen05._ksplit_for(M, N, K, n, 148) > 1
     rng = np.random.default_rng(7)
     A = [rng.standard_normal((M, K)).astype(np.float32) for _ in range(n)]
     B = [rng.standard_normal((K, N)).astype(np.float32) for _ in range(n)]
+    got = _run_dots(A, B)
+    for a, b, g in zip(A, B, got):
+        ref = a.astype(np.float64) @ b.astype(np.float64)
+        bound = 1e-4 * (np.abs(a).astype(np.float64) @ np.abs(b).astype(np.float64)) + 1e-5
+        assert np.all(np.abs(g - ref) <= bound)
+
+
+@pytest.mark.parametrize("shape,shares", [((300, 64, 200), [5]), ((256, 40, 96), [3, 3]),
+                                          ((512, 64, 4096), [4, 2, 3])])
+def test_n_fused_segments(shape, shares):
+    """Instances sharing A with narrow, distinct B run as N-fused segments
+    (one wide product per shared A); ragged M, N padded inside each block."""
+    from ad_b200 import tcgen05
+    M, N, K = shape
+    rng = np.random.default_rng(11)
+    A, B = [], []
+    for cnt in shares:
+        a = rng.standard_normal((M, K)).astype(np.float32)
+        for _ in range(cnt):
+            A.append(a)
+            B.append(rng.standard_normal((K, N)).astype(np.float32))
     got = _run_dots(A, B)
     for a, b, g in zip(A, B, got):
         ref = a.astype(np.float64) @ b.astype(np.float64)
@@ -169,13 +189,17 @@ def _run_dots(A, B):
     from ad_b200.device import CudaB200Device
     cmds, outs, ids = [], [], 1
     allocs = []
+    a_buf = {}                       # the same array object -> one shared buffer
     for a, b in zip(A, B):
         M, K = a.shape
         N = b.shape[1]
-        ia, ib, ic = ids, ids + 1, ids + 2
-        ids += 3
-        allocs += [ir.AllocEntry(ia, M * K, a.reshape(-1), False), ir.AllocEntry(ib, K * N, b.reshape(-1), False),
-                   ir.AllocEntry(ic, M * N, None, False)]
+        if id(a) not in a_buf:
+            a_buf[id(a)] = ids
+            allocs.append(ir.AllocEntry(ids, M * K, a.reshape(-1), False))
+            ids += 1
+        ia, ib, ic = a_buf[id(a)], ids, ids + 1
+        ids += 2
+        allocs += [ir.AllocEntry(ib, K * N, b.reshape(-1), False), ir.AllocEntry(ic, M * N, None, False)]
         ka = ir.KMatrix(ia, ir.Bin("Add", ir.Bin("Mult", ir.Xv(), ir.Const(K)), ir.Yv()), [M, K])
         kb = ir.KMatrix(ib, ir.Bin("Add", ir.Bin("Mult", ir.Xv(), ir.Const(N)), ir.Yv()), [K, N])
         kc = ir.KMatrix(ic, ir.Gid(), [M, N])
