@@ -59,8 +59,15 @@ def tile_n(N: int) -> int:
 
 def gen_split(karg: ir.KernelArg, name: str, rows: int, kdim: int, rows_p: int, k_p: int,
               row_var: str, k_var: str) -> KernelSpec:
-    """Gather operand(row, k) via its access expression into K-major hi/lo arrays.
-    ``row_var``/``k_var`` say which of the reference's X/Y carries row and k."""
+    """Gather operand(row, k) via its access expression into K-major hi/lo
+    arrays (``rows_p`` x ``k_p``, zero-padded).  ``row_var``/``k_var`` say which
+    of the reference's X/Y carries row and k.
+
+    One 256-thread block per 64 x 64 tile.  The operand is read along the axis
+    it is contiguous in (for a concatenation: the axis all of its pieces are
+    contiguous in) with 16-byte loads where the access is aligned, and through
+    a shared-memory transpose when that axis is the row axis; hi and lo are
+    written with 16-byte stores."""
     bufs = sorted({codegen.view_of(km, set()) for km in codegen._kmats_of(karg)})
     rng = {"X": (0, max(rows, kdim)), "Y": (0, max(rows, kdim)), "G": (0, 0)}
     it = "int"
@@ -70,47 +77,90 @@ def gen_split(karg: ir.KernelArg, name: str, rows: int, kdim: int, rows_p: int, 
     if rows_p * k_p >= (1 << 31) - 64:
         it = "long long"
     em = Emitter(bufs, it)
-    # read along whichever axis the data is contiguous in (for a concatenation:
-    # the axis all of its pieces are contiguous in)
     orient = "k"
     leaves = codegen._kmats_of(karg)
+    plain = isinstance(karg, ir.KMatrix) and not karg.is_temp
     if leaves and len(leaves) == len(_leaves(karg)):
         if all(exprs.lanes(km.access, k_var, 4).s == 1 for km in leaves):
             orient = "k"
         elif all(exprs.lanes(km.access, row_var, 4).s == 1 for km in leaves):
             orient = "r"
-    env = {row_var: "gr", k_var: "gk", "G": f"(({it})0)"}
-    val = em.scalar_karg(karg, env, {})
+    lane_var, other = (k_var, row_var) if orient == "k" else (row_var, k_var)
+    vec = plain and exprs.lanes(karg.access, lane_var, 4, {other: 1}).unit(4)
+    extent = kdim if orient == "k" else rows          # of the lane axis
     params = ", ".join([f"const float* __restrict__ p{i}" for i in range(len(bufs))] +
                        ["float* __restrict__ hi", "float* __restrict__ lo"])
+    # one float4 of the lane axis at (ga, gb): ga = lane-axis start, gb = other coordinate
+    coords = (lambda ga, gb: {k_var: ga, row_var: gb}) if orient == "k" else \
+        (lambda ga, gb: {row_var: ga, k_var: gb})
+    other_ext = rows if orient == "k" else kdim
+
+    def load4(dst: str, ga: str, gb: str) -> str:
+        env0 = dict(coords(ga, gb), G=f"(({it})0)")
+        lines = [f"float4 {dst} = make_float4(0.0f, 0.0f, 0.0f, 0.0f);",
+                 f"if ({gb} < ({it}){other_ext}) {{"]
+        if vec:
+            lines.append(f"    if ({ga} + 3 < ({it}){extent}) {dst} = "
+                         f"*reinterpret_cast<const float4*>(&{em.at(karg, env0)});")
+            lines.append("    else {")
+        else:
+            lines.append("    {")
+        for j, comp in enumerate("xyzw"):
+            envj = dict(coords(f"({ga} + {j})", gb), G=f"(({it})0)")
+            lines.append(f"        if ({ga} + {j} < ({it}){extent}) {dst}.{comp} = {em.scalar_karg(karg, envj, {})};")
+        lines.append("    }")
+        lines.append("}")
+        return "\n        ".join(lines)
+
+    split4 = """        unsigned h0, h1, h2, h3, l0, l1, l2, l3;
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h0) : "f"(v.x));
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h1) : "f"(v.y));
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h2) : "f"(v.z));
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h3) : "f"(v.w));
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l0) : "f"(v.x - __uint_as_float(h0)));
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l1) : "f"(v.y - __uint_as_float(h1)));
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l2) : "f"(v.z - __uint_as_float(h2)));
+        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l3) : "f"(v.w - __uint_as_float(h3)));
+        *reinterpret_cast<float4*>(&hi[o]) = make_float4(__uint_as_float(h0), __uint_as_float(h1),
+                                                         __uint_as_float(h2), __uint_as_float(h3));
+        *reinterpret_cast<float4*>(&lo[o]) = make_float4(__uint_as_float(l0), __uint_as_float(l1),
+                                                         __uint_as_float(l2), __uint_as_float(l3));"""
     if orient == "k":
-        load = f"""for (int i = threadIdx.y; i < 32; i += 8) {{
-        const {it} gr = r0 + i, gk = k0 + threadIdx.x;
-        t[i][threadIdx.x] = (gr < ({it}){rows} && gk < ({it}){kdim}) ? ({val}) : 0.0f;
+        body = f"""    #pragma unroll
+    for (int s = 0; s < 4; ++s) {{
+        const int idx = threadIdx.x + s * 256, row = idx >> 4, kq = (idx & 15) * 4;
+        const {it} gr = r0 + row, gk = k0 + kq;
+        if (gk >= ({it}){k_p}) continue;
+        {load4("v", "gk", "gr")}
+        const {it} o = gr * ({it}){k_p} + gk;
+{split4}
     }}"""
     else:
-        load = f"""for (int i = threadIdx.y; i < 32; i += 8) {{
-        const {it} gr = r0 + threadIdx.x, gk = k0 + i;
-        t[threadIdx.x][i] = (gr < ({it}){rows} && gk < ({it}){kdim}) ? ({val}) : 0.0f;
+        body = f"""    __shared__ float t[64][65];
+    #pragma unroll
+    for (int s = 0; s < 4; ++s) {{
+        const int idx = threadIdx.x + s * 256, kk = idx >> 4, rq = (idx & 15) * 4;
+        const {it} gk = k0 + kk, gr = r0 + rq;
+        {load4("u", "gr", "gk")}
+        t[kk][rq] = u.x; t[kk][rq + 1] = u.y; t[kk][rq + 2] = u.z; t[kk][rq + 3] = u.w;
+    }}
+    __syncthreads();
+    #pragma unroll
+    for (int s = 0; s < 4; ++s) {{
+        const int idx = threadIdx.x + s * 256, row = idx >> 4, kq = (idx & 15) * 4;
+        const {it} gr = r0 + row, gk = k0 + kq;
+        if (gk >= ({it}){k_p}) continue;
+        const float4 v = make_float4(t[kq][row], t[kq + 1][row], t[kq + 2][row], t[kq + 3][row]);
+        const {it} o = gr * ({it}){k_p} + gk;
+{split4}
     }}"""
     src = f"""extern "C" __global__ void __launch_bounds__(256) {name}({params}) {{
-    __shared__ float t[32][33];
-    const {it} r0 = ({it})blockIdx.y * 32, k0 = ({it})blockIdx.x * 32;
-    {load}
-    __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += 8) {{
-        const float x = t[i][threadIdx.x];
-        unsigned h, l;
-        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
-        const float r = x - __uint_as_float(h);
-        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(r));
-        const {it} o = (r0 + i) * ({it}){k_p} + k0 + threadIdx.x;
-        hi[o] = __uint_as_float(h);
-        lo[o] = __uint_as_float(l);
-    }}
+    const {it} r0 = ({it})blockIdx.y * 64, k0 = ({it})blockIdx.x * 64;
+{body}
 }}
 """
-    return KernelSpec(name, src, bufs, (k_p // 32, rows_p // 32, 1), (32, 8, 1), 0, "split",
+    assert rows_p % 64 == 0 and k_p % 4 == 0
+    return KernelSpec(name, src, bufs, (-(-k_p // 64), rows_p // 64, 1), (256, 1, 1), 0, "split",
                       4 * rows * kdim + 8 * rows_p * k_p)
 
 
@@ -699,7 +749,7 @@ extern "C" __global__ void __launch_bounds__(256) {name}(const unsigned long lon
 {chr(10).join(calls)}
 }}
 """
-    assert sa[0].block == sb[0].block == (32, 8, 1)
+    assert sa[0].block == sb[0].block == (256, 1, 1)
     sp = KernelSpec(name, src, [], (cbase, 1, 1), sa[0].block, 0, "split",
                     sum(x.bytes_moved for x in sa) + sum(x.bytes_moved for x in sb))
     sp.extra["table"] = rows
