@@ -420,7 +420,24 @@ def bench_loop(args, wl, rank, world, local, td):
     top = int(np.argmax(per_kernel))
     Lt = launches[top]
     hbm, bf16, peak_kind = peaks()
-    achieved = Lt.spec.bytes_moved / (max(per_kernel[top], 1e-9) / 1e3) / 1e9
+    kt = max(per_kernel[top], 1e-9) / 1e3
+    if Lt.spec.kind == "gemm_tcgen05" and not args.no_kernel_timing:
+        from ad_b200 import tcgen05
+        tf32 = tcgen05.measure_tf32_peak(ctx, dev.err_ptr)
+        achieved = 3 * Lt.spec.flops / kt / 1e12      # 3xTF32: three MMAs per product
+        roof = {"bound": "tensor", "achieved": achieved, "peak": tf32, "unit": "TFLOP/s",
+                "frac": achieved / tf32, "traffic": None,
+                "peak_kind": "measured: kind::tf32 tcgen05 probe in this run (smem-resident operands)",
+                "algorithmic_fp32_TFLOPs": Lt.spec.flops / kt / 1e12, "bf16_peak_measured": bf16}
+    else:
+        achieved = Lt.spec.bytes_moved / kt / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "traffic": None, "peak_kind": peak_kind}
+    roof.update({"kernel": f"{top}:{Lt.spec.kind}", "kernel_ms": float(per_kernel[top]),
+                 "alg_bytes": Lt.spec.bytes_moved})
+    work_set = dev.arena_bytes + getattr(dev, "scratch_bytes", 0)
+    l2_note = (f"step working set {work_set / 1e6:.0f} MB (arena + dot-operand scratch) "
+               + ("exceeds the 126 MB L2" if work_set > 126e6 else "fits in the 126 MB L2 (small model)"))
     feed_bytes = sum(4 * int(np.prod(c.shape)) for c in ir.iter_cmds(loop.proc) if type(c).__name__ == "Feeder")
     value = 1e3 / ms * (1 if dp else world)
     if rank == 0:
@@ -431,15 +448,11 @@ def bench_loop(args, wl, rank, world, local, td):
             "config": {"workload": case, "kernels_per_step": len(launches),
                        "global_batch": wl.get("global_batch"),
                        "step": "one ForNode iteration as a CUDA graph (Feeder H2D + kernels)",
-                       "l2": "working set fits in L2 (tiny model); launch-latency bound",
+                       "l2": l2_note,
                        "parallelism": (f"data parallel x{world} (NCCL all-reduce of gradients)" if dp
                                        else f"replicas x{world}")},
             "gpu_launches": len(launches) * args.steps,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": None, "peak_kind": peak_kind,
-                         "kernel": f"{top}:{Lt.spec.kind}", "kernel_ms": float(per_kernel[top]),
-                         "alg_bytes": Lt.spec.bytes_moved,
-                         "note": "latency-bound: kernels of a few microseconds"},
+            "roofline": roof,
             "per_kernel_ms": [round(float(x), 4) for x in per_kernel],
             "per_kernel_kind": [L.spec.kind for L in launches],
             "per_kernel_gflop": [round(L.spec.flops / 1e9, 3) for L in launches],
