@@ -471,13 +471,15 @@ def fuse_rows(proc: ir.Proc) -> ir.Proc:
 
 # ---------------------------------------------------------------- code generation
 
-STAGE_SMEM_MAX = 96 * 1024   # per block, both ring slots
+STAGE_SMEM_MAX = 96 * 1024   # per block, all ring slots
+# ring depth: 3 slots measured slower than 2 on config 2 (4358 vs ~4550 GB/s)
+MAX_SLOTS = 2
 
 
 def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int = 148) -> KernelSpec:
     """Two schedules.  *Staged* (one row per thread group, rows streamed): a
     persistent loop over rows in which thread 0 prefetches the next row's
-    row-canonical inputs with ``cp.async.bulk`` (TMA, 1-D) into a 2-slot
+    row-canonical inputs with ``cp.async.bulk`` (TMA, 1-D) into a ``MAX_SLOTS``-slot
     shared-memory ring while the block computes the current row.  *Direct*
     (short rows, several rows per block): inputs are loaded straight from
     global memory."""
@@ -511,7 +513,9 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
     kinds = st_run.kinds
     staged = sorted(b for b, pat in st_run.read_pattern.items()
                     if pat == "row" and b not in kinds and b not in rf.internal)
-    stage_bytes = 2 * len(staged) * R * 4
+    slot_bytes = len(staged) * R * 4
+    nslot = max(2, min(MAX_SLOTS, STAGE_SMEM_MAX // max(slot_bytes, 1)))
+    stage_bytes = nslot * slot_bytes
     staged_mode = rows_pb == 1 and staged and stage_bytes <= STAGE_SMEM_MAX
     if not staged_mode:
         staged = []
@@ -794,14 +798,14 @@ __device__ __noinline__ bool rf_wait(unsigned long long* b, unsigned ph) {{
 extern "C" __global__ void __launch_bounds__({block}) {name}({params}) {{
     extern __shared__ __align__(128) float4 stg[];
     __shared__ float red[2][{max_group}][{nw_tot}];
-    __shared__ __align__(8) unsigned long long bar[2];
+    __shared__ __align__(8) unsigned long long bar[{nslot}];
     const int tig = threadIdx.x;
     const int grp = 0;
     (void)grp;
     const bool live = true;
     if (threadIdx.x == 0) {{
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(rf_smem(&bar[0])));
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(rf_smem(&bar[1])));
+        for (int s = 0; s < {nslot}; ++s)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(rf_smem(&bar[s])));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }}
     __syncthreads();
@@ -810,17 +814,23 @@ extern "C" __global__ void __launch_bounds__({block}) {name}({params}) {{
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(rf_smem(&bar[s])), "r"({len(staged) * row_bytes}u) : "memory");
             {issue}
     }};
-    if (threadIdx.x == 0 && ({it})blockIdx.x < ({it}){V}) issue(0, ({it})blockIdx.x);
+    // ring of {nslot} slots: row i of this block goes to slot i % {nslot}, {nslot - 1} rows ahead
+    if (threadIdx.x == 0)
+        for (int j = 0; j < {nslot - 1}; ++j)
+            if (({it})blockIdx.x + ({it})j * gridDim.x < ({it}){V}) issue(j, ({it})blockIdx.x + ({it})j * gridDim.x);
     int iter = 0;
     for ({it} xr = blockIdx.x; xr < ({it}){V}; xr += gridDim.x, ++iter) {{
-        const int slot = iter & 1;
-        const {it} nxt = xr + gridDim.x;
-        if (threadIdx.x == 0 && nxt < ({it}){V}) issue(slot ^ 1, nxt);
-        const bool ok = __syncthreads_and(rf_wait(&bar[slot], (iter >> 1) & 1));
+        const int slot = iter % {nslot};
+        const {it} nxt = xr + ({it}){nslot - 1} * gridDim.x;
+        if (threadIdx.x == 0 && nxt < ({it}){V}) issue((iter + {nslot - 1}) % {nslot}, nxt);
+        const bool ok = __syncthreads_and(rf_wait(&bar[slot], (iter / {nslot}) & 1));
         if (!ok) {{
             if (threadIdx.x == 0) {{
                 atomicExch(err, 5);
-                if (nxt < ({it}){V}) rf_wait(&bar[slot ^ 1], ((iter + 1) >> 1) & 1);
+                // bounded drain of the copies still in flight before the block exits
+                for (int j = 1; j < {nslot}; ++j)
+                    if (xr + ({it})j * gridDim.x < ({it}){V})
+                        rf_wait(&bar[(iter + j) % {nslot}], ((iter + j) / {nslot}) & 1);
             }}
             break;
         }}
