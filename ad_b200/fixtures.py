@@ -40,10 +40,13 @@ def _make_full(spec: Dict) -> np.ndarray:
     raise ValueError(spec["dist"])
 
 
-def load_case(case: str, path: Optional[str] = None, with_content: bool = True, rank: int = 0):
+def load_case(case: str, path: Optional[str] = None, with_content: bool = True, rank: int = 0,
+              feeder_seed_offset: int = 0):
     """Returns ``(proc, meta)`` with every AllocEntry content materialised.  For a
     data-parallel fixture (``meta["dp_parts"] > 1``) ``rank`` picks that rank's rows
-    of the per-example data (inputs and the fixed loss weights)."""
+    of the per-example data (inputs and the fixed loss weights).
+    ``feeder_seed_offset`` shifts the seeds of the Feeders' data only (weights
+    unchanged): each rank of a weak-scaling data-parallel run feeds its own batch."""
     proc, meta = ir.load_proc(path or os.path.join(PROC_DIR, f"{case}.json.gz"))
 
     def with_rank(sp):
@@ -61,7 +64,10 @@ def load_case(case: str, path: Optional[str] = None, with_content: bool = True, 
                 val, shape = f["fill"], tuple(f["shape"])
                 c.func = lambda val=val, shape=shape: np.full(shape, val, dtype=np.float32)
             elif f is not None and "spec" in f:
-                arr = make_array(with_rank(f["spec"]))
+                sp = with_rank(f["spec"])
+                if feeder_seed_offset and "seed" in sp:
+                    sp = dict(sp, seed=sp["seed"] + feeder_seed_offset)
+                arr = make_array(sp)
                 c.func = lambda arr=arr: arr
     return proc, meta
 

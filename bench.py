@@ -41,6 +41,10 @@ WORKLOADS = {
             "metric": "encoder train steps/s (4 layers, d512, 8 heads, ff2048, S128, B32, fp32, SGD)",
             "unit": "steps/s", "loop": True, "cpu_iters": 1, "dp": True, "global_batch": 32,
             "data": "synthetic: x ~ N(0,1) [4096, 512] seed 0 via Feeder; Xavier-uniform weights (seeded)"},
+    "enc_weak": {"case": "enc_4_32_128_512_8_2048_100",
+                 "metric": "encoder train sequences/s (4 layers, d512, 8 heads, ff2048, S128, batch 32 per GPU, fp32, SGD)",
+                 "unit": "sequences/s", "loop": True, "cpu_iters": 1, "dp": "weak", "batch_per_gpu": 32,
+                 "data": "synthetic: x ~ N(0,1) [4096, 512] per rank (seed 1000*rank) via Feeder; Xavier-uniform weights (seeded, same on every rank)"},
     "enc_small": {"case": "enc_1_8_128_512_8_2048_100",
                   "metric": "encoder train steps/s (1 layer, d512, 8 heads, ff2048, S128, B8, fp32, SGD)",
                   "unit": "steps/s", "loop": True, "cpu_iters": 1,
@@ -377,14 +381,18 @@ def bench_loop(args, wl, rank, world, local, td):
     from ad_b200.fixtures import load_case, set_loop_count
     case = wl["case"]
     dp = None
+    weak = wl.get("dp") == "weak"
     if world > 1 and wl.get("dp"):
-        # data parallel: this rank's shard of the global batch, gradients summed with NCCL
-        case = f"{case}_p{world}"
+        # data parallel, gradients summed with NCCL.  Strong: this rank's shard of
+        # the fixed global batch.  Weak: the full per-GPU batch on every rank, each
+        # with its own data (global batch = batch_per_gpu x world).
+        if not weak:
+            case = f"{case}_p{world}"
         from ad_b200 import dist
         box = [dist.nccl_unique_id() if rank == 0 else None]
         td.broadcast_object_list(box, src=0)
         dp = (rank, world, box[0])
-    p, meta = load_case(case, rank=rank)
+    p, meta = load_case(case, rank=rank, feeder_seed_offset=1000 * rank if weak else 0)
     set_loop_count(p, args.warmup)
     dev = CudaB200Device(local, dp=dp)
     proc = dev.prepare(p)
@@ -439,14 +447,17 @@ def bench_loop(args, wl, rank, world, local, td):
     l2_note = (f"step working set {work_set / 1e6:.0f} MB (arena + dot-operand scratch) "
                + ("exceeds the 126 MB L2" if work_set > 126e6 else "fits in the 126 MB L2 (small model)"))
     feed_bytes = sum(4 * int(np.prod(c.shape)) for c in ir.iter_cmds(loop.proc) if type(c).__name__ == "Feeder")
-    value = 1e3 / ms * (1 if dp else world)
+    if weak:
+        value = 1e3 / ms * wl["batch_per_gpu"] * world       # sequences per second, whole job
+    else:
+        value = 1e3 / ms * (1 if dp else world)
     if rank == 0:
         line = {
             "metric": wl["metric"], "value": value, "unit": wl["unit"], "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong" if dp else "weak", "vs_baseline": None, "dtype": "f32", "data": wl["data"],
+            "scaling": "strong" if (dp and not weak) else "weak", "vs_baseline": None, "dtype": "f32", "data": wl["data"],
             "config": {"workload": case, "kernels_per_step": len(launches),
-                       "global_batch": wl.get("global_batch"),
+                       "global_batch": wl.get("global_batch") or wl.get("batch_per_gpu", 0) * world or None,
                        "step": "one ForNode iteration as a CUDA graph (Feeder H2D + kernels)",
                        "l2": l2_note,
                        "parallelism": (f"data parallel x{world} (NCCL all-reduce of gradients)" if dp
@@ -481,7 +492,8 @@ def cpu_loop_baseline(wl):
     t0 = time.perf_counter()
     d.run_proc(d.proc)
     dt = time.perf_counter() - t0
-    return {"value": n / dt, "unit": wl["unit"], "cores": threads, "kind": "port",
+    per_step = wl.get("batch_per_gpu", 1) if wl["unit"] == "sequences/s" else 1
+    return {"value": n * per_step / dt, "unit": wl["unit"], "cores": threads, "kind": "port",
             "sample": f"{n} iterations of {wl['case']} (C restatement of the reference kernels, OpenMP x{threads})"}
 
 
