@@ -822,21 +822,22 @@ extern "C" __global__ void __launch_bounds__({block}) {name}({params}) {{
     for ({it} xr = blockIdx.x; xr < ({it}){V}; xr += gridDim.x, ++iter) {{
         const int slot = iter % {nslot};
         const {it} nxt = xr + ({it}){nslot - 1} * gridDim.x;
-        if (threadIdx.x == 0 && nxt < ({it}){V}) issue((iter + {nslot - 1}) % {nslot}, nxt);
+        // this barrier also ends every thread's use of the previous row's slot, which
+        // the prefetch below overwrites (so no barrier is needed at the end of a row)
         const bool ok = __syncthreads_and(rf_wait(&bar[slot], (iter / {nslot}) & 1));
         if (!ok) {{
             if (threadIdx.x == 0) {{
                 atomicExch(err, 5);
                 // bounded drain of the copies still in flight before the block exits
-                for (int j = 1; j < {nslot}; ++j)
+                for (int j = 1; j < {nslot - 1}; ++j)
                     if (xr + ({it})j * gridDim.x < ({it}){V})
                         rf_wait(&bar[(iter + j) % {nslot}], ((iter + j) / {nslot}) & 1);
             }}
             break;
         }}
+        if (threadIdx.x == 0 && nxt < ({it}){V}) issue((iter + {nslot - 1}) % {nslot}, nxt);
         const {it} rowbase = xr * ({it}){R};
         {body}
-        __syncthreads();
     }}
 }}
 """
