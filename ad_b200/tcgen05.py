@@ -437,14 +437,18 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
 """
 
 
-def choose_ksplit(units: int, kblocks: int, sm_count: int) -> int:
+def choose_ksplit(units: int, kblocks: int, sm_count: int, bn: int = 256) -> int:
     """K slices per output tile: minimise waves x (K blocks per slice + pipeline
-    fill), at least 4 K blocks per slice, a small cost per extra slice for the
-    partial sums' round trip."""
+    fill), at least 4 K blocks per slice.  More than one slice adds the partial
+    sums' round trip and the summing kernel's launch, about 8 us, charged in K
+    blocks of this tile width (one K block of a 128 x bn tile is 3 MMAs of
+    128 x bn x 16 at ~7.3 TFLOP/s per SM)."""
+    kblock_us = 3 * 2 * 128 * bn * BKF / 7.3e12 * 1e6
+    penalty = -(-8.0 // kblock_us)
     best, best_cost = 1, None
     for s_ in range(1, min(32, kblocks // 4) + 1):
         waves = -(-units * s_ // sm_count)
-        cost = waves * (-(-kblocks // s_) + 6) + (2 if s_ > 1 else 0)
+        cost = waves * (-(-kblocks // s_) + 6) + (penalty if s_ > 1 else 0)
         if best_cost is None or cost < best_cost:
             best, best_cost = s_, cost
     return best
@@ -666,7 +670,7 @@ class GroupPlan:
         else:
             self.bn = bn0
             units = n * mblk * (self.Np // bn0)
-        self.ks = choose_ksplit(units, self.Kp // BKF, sm_count)
+        self.ks = choose_ksplit(units, self.Kp // BKF, sm_count, self.bn)
         self.raw = self.ks > 1 or heavy_epilogue(cmds[0], units, sm_count)
 
     def _dedupe(self, cmds, which: int, name: str):
