@@ -21,6 +21,7 @@ import argparse
 import json
 import math
 import os
+import re
 import subprocess
 import sys
 import threading
@@ -33,7 +34,8 @@ sys.path.insert(0, ROOT)
 
 WORKLOADS = {
     "lnsm": {"case": "lnsm_8192_4096", "data": "synthetic: x ~ N(0,1) seed 0, dy ~ N(0,1) seed 1 (numpy default_rng)", "metric": "fused-kernel HBM GB/s (LayerNorm+softmax fwd+bwd, fp32 [8192,4096])",
-             "unit": "GB/s", "min_bytes": 4 * 8192 * 4096 * 4},
+             "unit": "GB/s", "min_bytes": 4 * 8192 * 4096 * 4,
+             "profile": ("rowfused", "rowfused_lnsm_8192x4096.md")},
     "mlp": {"case": "mlp", "metric": "Linear MLP train steps/s (examples/linear.py: 255-255-255, batch 2, SGD)",
             "unit": "steps/s", "loop": True, "cpu_iters": 300,
             "data": "Feeder of np.full((2,255), 0.2); weights from np.random.seed(0) randn (reference init)"},
@@ -51,8 +53,30 @@ WORKLOADS = {
                   "data": "synthetic: x ~ N(0,1) [1024, 512] seed 0 via Feeder; Xavier-uniform weights (seeded)"},
     "dotsig": {"case": "dotsig_4096", "data": "synthetic: X, W, b ~ U(-1/64, 1/64), dz ~ N(0,1), seeded numpy default_rng", "metric": "fused DotProd+sigmoid fwd+bwd TFLOP/s (fp32 4096^3)",
                "unit": "TFLOP/s", "flops": 3 * 2 * 4096 ** 3, "inputs": ("X_id", "dz_id"),
-               "cpu_dot_rows": 16, "dot_m": 4096},
+               "cpu_dot_rows": 16, "dot_m": 4096,
+               "profile": ("gemm_tcgen05", "gemm_tcgen05_dotsig_4096.md")},
 }
+
+
+def profile_traffic(wl, kind):
+    """DRAM bytes (read + write) per launch of the dominant kernel, from the
+    committed ncu summary of that kernel on this workload (one ncu capture of
+    the same bench command; ``dram__bytes_read.sum`` + ``dram__bytes_write.sum``)."""
+    prof = wl.get("profile")
+    if not prof or prof[0] != kind:
+        return None, None
+    path = os.path.join(ROOT, "profiles", prof[1])
+    if not os.path.exists(path):
+        return None, None
+    units = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}
+    total, seen = 0.0, 0
+    with open(path) as f:
+        for line in f:
+            m = re.match(r"\|\s*dram__bytes_(read|write)\.sum\s*\|\s*([0-9.]+)\s*(\w+)", line)
+            if m and m.group(3) in units:
+                total += float(m.group(2)) * units[m.group(3)]
+                seen += 1
+    return (int(total), f"profiles/{prof[1]} (ncu)") if seen == 2 else (None, None)
 
 
 def peaks():
@@ -291,11 +315,7 @@ def main():
     hbm, bf16, peak_kind = peaks()
     top = int(np.argmax(per_kernel))
     Lt = launches[top]
-    traffic = None
-    tfile = os.path.join(ROOT, "profiles", f"traffic_{wl['case']}.json")
-    if os.path.exists(tfile):
-        with open(tfile) as f:
-            traffic = json.load(f).get(Lt.spec.kind)
+    traffic, traffic_src = profile_traffic(wl, Lt.spec.kind)
     if Lt.spec.kind == "gemm_tcgen05":
         from ad_b200 import tcgen05
         tf32 = tcgen05.measure_tf32_peak(ctx, dev.err_ptr)
@@ -311,7 +331,7 @@ def main():
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind}
     roof.update({"kernel": f"{top}:{Lt.spec.kind}", "kernel_ms": float(per_kernel[top]),
-                 "alg_bytes": Lt.spec.bytes_moved})
+                 "alg_bytes": Lt.spec.bytes_moved, "traffic_source": traffic_src})
 
     # e2e through the public API with host-resident inputs (pinned)
     in_ids = [meta[k] for k in wl.get("inputs", ("x_id", "dy_id")) if k in meta]
