@@ -441,9 +441,11 @@ def choose_ksplit(units: int, kblocks: int, sm_count: int, bn: int = 256) -> int
     """K slices per output tile: minimise waves x (K blocks per slice + pipeline
     fill), at least 4 K blocks per slice.  More than one slice adds the partial
     sums' round trip and the summing kernel's launch, about 8 us, charged in K
-    blocks of this tile width (one K block of a 128 x bn tile is 3 MMAs of
-    128 x bn x 16 at ~7.3 TFLOP/s per SM)."""
-    kblock_us = 3 * 2 * 128 * bn * BKF / 7.3e12 * 1e6
+    blocks.  A K block takes ~0.43 us whatever the tile width up to 256 (the
+    4096^3 product ran 1024 tiles of 128 x 128 at the same time per K block as
+    512 tiles of 128 x 256): the stage pipeline, not the MMA, sets it, which is
+    also why the widest tile is always used."""
+    kblock_us = 0.43
     penalty = -(-8.0 // kblock_us)
     best, best_cost = 1, None
     for s_ in range(1, min(32, kblocks // 4) + 1):
