@@ -47,11 +47,6 @@ WORKLOADS = {
                  "metric": "encoder train sequences/s (4 layers, d512, 8 heads, ff2048, S128, batch 32 per GPU, fp32, SGD)",
                  "unit": "sequences/s", "loop": True, "cpu_iters": 1, "dp": "weak", "batch_per_gpu": 32,
                  "data": "synthetic: x ~ N(0,1) [4096, 512] per rank (seed 1000*rank) via Feeder; Xavier-uniform weights (seeded, same on every rank)"},
-    "enc12": {"case": "enc_12_256_512_1024_16_4096_50_p8",
-              "metric": "encoder train sequences/s (12 layers, d1024, 16 heads, ff4096, S512, batch 32 per GPU, fp32, SGD)",
-              "unit": "sequences/s", "loop": True, "cpu_iters": 0, "dp": "weak", "batch_per_gpu": 32,
-              "rank_rows": True,
-              "data": "synthetic: global x ~ N(0,1) [256*512, 1024] seed 0, rank r feeds rows of sequences 32r..32r+31; Xavier-uniform weights (seeded)"},
     "enc_small": {"case": "enc_1_8_128_512_8_2048_100",
                   "metric": "encoder train steps/s (1 layer, d512, 8 heads, ff2048, S128, B8, fp32, SGD)",
                   "unit": "steps/s", "loop": True, "cpu_iters": 1,
@@ -422,9 +417,8 @@ def bench_loop(args, wl, rank, world, local, td):
         box = [dist.nccl_unique_id() if rank == 0 else None]
         td.broadcast_object_list(box, src=0)
         dp = (rank, world, box[0])
-    # weak scaling: each rank its own data -- its rows of the seeded global batch for a
-    # per-rank fixture ("rank_rows"), else the same fixture with a rank-shifted seed
-    offset = 1000 * rank if (weak and not wl.get("rank_rows")) else 0
+    # weak scaling: each rank feeds its own batch (the fixture's seed shifted by rank)
+    offset = 1000 * rank if weak else 0
     p, meta = load_case(case, rank=rank, feeder_seed_offset=offset)
     set_loop_count(p, args.warmup)
     dev = CudaB200Device(local, dp=dp)
