@@ -737,8 +737,18 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
             for ai, acc in enumerate(accs):
                 lines.append(f"if ((threadIdx.x & 31) == 0) red[{slot_r}][{ai}][threadIdx.x >> 5] = {acc};")
             lines.append("__syncthreads();")
+            nw_all = max(1, block // 32)
             for ai, (acc, comb) in enumerate(zip(accs, combs)):
-                parts = [f"red[{slot_r}][{ai}][grp * {nw} + {i}]" for i in range(nw)]
+                if nw % 4 == 0 and nw_all % 4 == 0:
+                    # 16-byte reads of the warp partials, summed in the same order
+                    parts = []
+                    for q4 in range(nw // 4):
+                        v = f"rq{n_red}_{ai}_{q4}"
+                        lines.append(f"const float4 {v} = *reinterpret_cast<const float4*>"
+                                     f"(&red[{slot_r}][{ai}][grp * {nw} + {4 * q4}]);")
+                        parts += [f"{v}.x", f"{v}.y", f"{v}.z", f"{v}.w"]
+                else:
+                    parts = [f"red[{slot_r}][{ai}][grp * {nw} + {i}]" for i in range(nw)]
                 tot = parts[0]
                 for pp in parts[1:]:
                     tot = comb(tot, pp)
@@ -754,7 +764,7 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
     if not staged_mode:
         body = "\n    ".join(body_lines)
         src = f"""extern "C" __global__ void __launch_bounds__({block}) {name}({params}) {{
-    __shared__ float red[2][{max_group}][{nw_tot}];
+    __shared__ __align__(16) float red[2][{max_group}][{nw_tot}];
     const int tig = threadIdx.x % {gs};
     const int grp = threadIdx.x / {gs};
     (void)grp; (void)red; (void)err;
@@ -797,7 +807,7 @@ __device__ __noinline__ bool rf_wait(unsigned long long* b, unsigned ph) {{
 
 extern "C" __global__ void __launch_bounds__({block}) {name}({params}) {{
     extern __shared__ __align__(128) float4 stg[];
-    __shared__ float red[2][{max_group}][{nw_tot}];
+    __shared__ __align__(16) float red[2][{max_group}][{nw_tot}];
     __shared__ __align__(8) unsigned long long bar[{nslot}];
     const int tig = threadIdx.x;
     const int grp = 0;
