@@ -673,7 +673,7 @@ class GroupPlan:
             self.bn = bn0
             units = n * mblk * (self.Np // bn0)
         self.ks = choose_ksplit(units, self.Kp // BKF, sm_count, self.bn)
-        self.raw = self.ks > 1 or heavy_epilogue(cmds[0], units, sm_count)
+        self.raw = self.ks > 1 or heavy_epilogue(cmds[0], n, units, self.Kp // BKF, sm_count)
 
     def _dedupe(self, cmds, which: int, name: str):
         rows, rows_p, rv, kv = ((self.M, self.Mp, "X", "Y") if which == 0 else (self.N, self.Np, "Y", "X"))
@@ -699,16 +699,23 @@ def group_scratch_bytes(cmds, sm_count: int = 148) -> int:
     return GroupPlan(cmds, sm_count).scratch_bytes()
 
 
-def heavy_epilogue(c, tiles: int, sm_count: int) -> bool:
-    """Run the fused epilogue as its own kernel when it reads much more than the
-    product itself (more than 4 extra floats per output: e.g. the sum of every
-    head's input gradient fused into one head's dot) and the GEMM's ``tiles``
-    would leave SMs idle: the GEMM's epilogue warps on a few SMs cannot pull
-    that traffic, a kernel over the whole GPU can."""
+def heavy_epilogue(c, n_inst: int, units: int, kblocks: int, sm_count: int) -> bool:
+    """Run the fused epilogue as its own kernel when that is estimated faster.
+    Inside the GEMM the epilogue warps (8 per SM) sustain ~1.5 TB/s (measured:
+    the 4096 x 2048 x 512 FFN product with bias + ReLU takes 43 us for 67 MB of
+    epilogue traffic), overlapped with the main loop; a separate kernel over
+    the whole GPU streams ~5 TB/s but adds the raw product's round trip
+    (8 bytes per output) and a launch.  Epilogues that read much more than the
+    product (the sum of every head's input gradient fused into one head's dot)
+    or short-K products with read-heavy epilogues (attention backward) go
+    separate."""
     dn, M, N, K = dot_shape(c)
     rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
-    epi_bytes = codegen.written_reads_bytes(_epi_only(c), rngw, {})
-    return tiles < 2 * sm_count and epi_bytes > 4 * 6 * M * N
+    epi = n_inst * codegen.written_reads_bytes(_epi_only(c), rngw, {})
+    main_us = -(-units // sm_count) * (kblocks + 6) * 0.43
+    fused_us = max(main_us, epi / 1.5e6)
+    sep_us = main_us + (epi + 8 * n_inst * M * N) / 5.0e6 + 8.0
+    return sep_us < fused_us
 
 
 _KSIG = re.compile(r'extern "C" __global__ void __launch_bounds__\(256\) (\w+)\(([^)]*)\)\s*\{')

@@ -47,6 +47,10 @@ WORKLOADS = {
                  "metric": "encoder train sequences/s (4 layers, d512, 8 heads, ff2048, S128, batch 32 per GPU, fp32, SGD)",
                  "unit": "sequences/s", "loop": True, "cpu_iters": 1, "dp": "weak", "batch_per_gpu": 32,
                  "data": "synthetic: x ~ N(0,1) [4096, 512] per rank (seed 1000*rank) via Feeder; Xavier-uniform weights (seeded, same on every rank)"},
+    "enc3_d1024": {"case": "enc_3_96_512_1024_16_4096_50_p3",
+                   "metric": "encoder train sequences/s (3 layers, d1024, 16 heads, ff4096, S512, batch 32 per GPU, fp32, SGD)",
+                   "unit": "sequences/s", "loop": True, "cpu_iters": 0, "dp": "weak", "batch_per_gpu": 32,
+                   "data": "synthetic: x ~ N(0,1) [32*512, 1024] per rank (seed 1000*rank) via Feeder; Xavier-uniform weights (seeded, same on every rank)"},
     "enc_small": {"case": "enc_1_8_128_512_8_2048_100",
                   "metric": "encoder train steps/s (1 layer, d512, 8 heads, ff2048, S128, B8, fp32, SGD)",
                   "unit": "steps/s", "loop": True, "cpu_iters": 1,
@@ -419,7 +423,7 @@ def bench_loop(args, wl, rank, world, local, td):
         dp = (rank, world, box[0])
     # weak scaling: each rank feeds its own batch (the fixture's seed shifted by rank)
     offset = 1000 * rank if weak else 0
-    p, meta = load_case(case, rank=rank, feeder_seed_offset=offset)
+    p, meta = load_case(case, rank=0 if weak else rank, feeder_seed_offset=offset)
     set_loop_count(p, args.warmup)
     dev = CudaB200Device(local, dp=dp)
     proc = dev.prepare(p)
