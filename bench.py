@@ -498,6 +498,8 @@ def bench_loop(args, wl, rank, world, local, td):
             "per_kernel_ms": [round(float(x), 4) for x in per_kernel],
             "per_kernel_kind": [L.spec.kind for L in launches],
             "per_kernel_gflop": [round(L.spec.flops / 1e9, 3) for L in launches],
+            "per_kernel_GBps": [round(L.spec.bytes_moved / (t / 1e3) / 1e9, 1) if t > 0 else None
+                                for L, t in zip(launches, per_kernel)],
             "clocks": clk.summary(),
             "e2e": {"value": value, "unit": wl["unit"], "h2d_bytes_per_step": feed_bytes,
                     "d2h_bytes_per_step": 0,
