@@ -432,6 +432,13 @@ class CudaB200Device:
         the generated kernel source (tensor-core dots: split + GEMM sources)."""
         if type(c).__name__ not in ir.COMPUTE_KINDS:
             return None
+        cache = self.__dict__.setdefault("_sig_cache", {})
+        if id(c) in cache:
+            return cache[id(c)]
+        cache[id(c)] = sig = self._batch_signature(c, sizes)
+        return sig
+
+    def _batch_signature(self, c, sizes: Dict[int, int]) -> Optional[str]:
         sp = self._single_spec(c, sizes)
         if sp is None and type(c).__name__ in DOT:
             from . import gemm

@@ -448,15 +448,13 @@ def fuse_rows(proc: ir.Proc) -> ir.Proc:
                 rr |= rws[m][0]
                 ww |= rws[m][1]
             mset = set(members)
-            new_seq, new_rws = [], []
-            for k, c in enumerate(seq):
-                if k == P:
-                    new_seq.append(rf)
-                    new_rws.append((rr, ww))
-                elif k not in mset:
-                    new_seq.append(c)
-                    new_rws.append(rws[k])
-            seq, rws = new_seq, new_rws
+            assert P in mset
+            # splice in place: the run takes its anchor's slot, the other members go
+            seq[P] = rf
+            rws[P] = (rr, ww)
+            for k in sorted(mset - {P}, reverse=True):
+                del seq[k]
+                del rws[k]
             changed = True
             # the anchor slot now holds the next command (or the run itself)
         if not changed:
