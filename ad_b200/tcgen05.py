@@ -594,22 +594,39 @@ def gen_splitk_epilogue(c, name: str, M: int, N: int, ksplit: int, n_inst: int =
         ptrs = "\n    ".join(
             f"float* __restrict__ p{i} = reinterpret_cast<float*>(ad_tab[(unsigned)inst * {tabw}u + {2 + i}u]);"
             for i in range(len(bufs)))
+    epi = "\n        ".join(epi.split("\n"))
+    # 4 outputs per thread, in four contiguous 256-output chunks per block: every load
+    # instruction stays coalesced and each thread keeps 4x the loads in flight
     src = f"""extern "C" __global__ void __launch_bounds__(256) {name}({params}const float* __restrict__ ad_ws) {{
     const int inst = blockIdx.z;
-    const long long e = (long long)blockIdx.x * 256 + threadIdx.x;
-    if (e >= {M * N}ll) return;
+    const long long base = (long long)blockIdx.x * 1024 + threadIdx.x;
+    if (base >= {M * N}ll) return;
     {ptrs}
-    const {it} om = ({it})(e / {N}), on = ({it})(e % {N});
-    const float* w = ad_ws + (long long)inst * {ksplit * M * N}ll + e;
-    float accv = 0.0f;
+    const float* w = ad_ws + (long long)inst * {ksplit * M * N}ll;
+    float accs[4];
     #pragma unroll
-    for (int s = 0; s < {ksplit}; ++s) accv += w[(long long)s * {M * N}ll];
-    {epi}
+    for (int j = 0; j < 4; ++j) {{
+        const long long e = base + j * 256;
+        float a = 0.0f;
+        if (e < {M * N}ll) {{
+            #pragma unroll
+            for (int s = 0; s < {ksplit}; ++s) a += w[(long long)s * {M * N}ll + e];
+        }}
+        accs[j] = a;
+    }}
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {{
+        const long long e = base + j * 256;
+        if (e >= {M * N}ll) break;
+        const {it} om = ({it})(e / {N}), on = ({it})(e % {N});
+        const float accv = accs[j];
+        {epi}
+    }}
 }}
 """
     rngw = {"X": (0, M - 1), "Y": (0, N - 1), "G": (0, M * N - 1)}
     epi_bytes = codegen.written_reads_bytes(_epi_only(c), rngw, {})
-    spec = KernelSpec(name, src, bufs if n_inst == 1 else [], (-(-M * N // 256), 1, n_inst), (256, 1, 1), 0,
+    spec = KernelSpec(name, src, bufs if n_inst == 1 else [], (-(-M * N // 1024), 1, n_inst), (256, 1, 1), 0,
                       "splitk_epilogue", n_inst * (4 * ksplit * M * N + epi_bytes))
     return spec
 
