@@ -2,26 +2,31 @@
 
 Reference semantics: ``C[ty,tx] = sum_k A(_x=ty,_y=k) * B(_x=k,_y=tx)`` in fp32
 (autodiff/device/opencl/kernels/dotprod.py:7-43) with the fused epilogue of
-dp_elw_fuse.py:11-65.  B200 schedule, three launches per dot:
+dp_elw_fuse.py:11-65.  B200 schedule for one dot command, or for a group of
+dot commands whose kernels differ only in their buffers (``GroupPlan``):
 
-1. ``split A`` / ``split B``: gather each operand through its access
-   expression (any folded Permute/View/Broadcast/Concat, or a constant),
-   transposing through shared memory when the operand is MN-contiguous, and
-   write it K-major, zero-padded to the tile grid, as two fp32 arrays:
-   ``hi = tf32_rn(x)`` and ``lo = tf32_rn(x - hi)``.
-2. ``gemm``: one CTA per 128 x BN output tile.  Warp 0 lane 0 issues TMA
-   loads (SWIZZLE_128B, 32 fp32 of K per row) of A_hi, A_lo, B_hi, B_lo into a
-   ``STAGES``-deep ring; warp 1 lane 0 issues, per 8-deep K slice,
-   ``A_hi*B_hi + A_hi*B_lo + A_lo*B_hi`` as three ``tcgen05.mma.kind::tf32``
-   into one fp32 TMEM accumulator (the published 3xTF32 split; the dropped
-   ``lo*lo`` term is below fp32 rounding), and ``tcgen05.commit`` releases each
-   stage.  All four warps then read TMEM (``tcgen05.ld.32x32b.x32``),
-   transpose 32x32 blocks through shared memory so that stores are coalesced,
-   and run the fused elementwise epilogue per element.
+1. ``split`` (one launch): gather every distinct A and B operand through its
+   access expression (any folded Permute/View/Broadcast/Concat, or a
+   constant) and write it K-major, zero-padded to the tile grid, as two fp32
+   arrays ``hi = tf32_rn(x)`` and ``lo = tf32_rn(x - hi)``; operands of a
+   group are stacked, operands shared by several members are split once.
+2. ``gemm``: a persistent, warp-specialised kernel over all work units (tile x
+   K slice x member).  Warp 0 lane 0 issues TMA loads (16 fp32 of K per row,
+   SWIZZLE_64B) of A_hi, A_lo, B_hi, B_lo into a 4-stage ring; warp 1 lane 0
+   issues, per 8-deep K slice, ``A_hi*B_hi + A_hi*B_lo + A_lo*B_hi`` as three
+   ``tcgen05.mma.kind::tf32`` into a TMEM accumulator (the published 3xTF32
+   split; the dropped ``lo*lo`` term is below fp32 rounding), with two
+   accumulators so the epilogue of one tile overlaps the next tile's MMAs;
+   warps 2-9 read TMEM (``tcgen05.ld.32x32b.x32``), transpose 32x32 blocks
+   through shared memory for coalesced stores, and run the fused epilogue.
+   Members sharing A with narrow B run as N-fused segments (one wide
+   product per shared A).
+3. ``splitk_epilogue`` (only when K is split or the epilogue is estimated
+   faster on its own): sums the K slices in order and runs the epilogue.
 
 Every mbarrier wait is bounded; on timeout the kernel records an error code
-in a device flag, stops issuing work, frees its TMEM and returns.
-No TMA multicast is used anywhere.
+in a device flag, stops issuing work, drains its copies, frees its TMEM and
+returns.  No TMA multicast is used anywhere.
 """
 from __future__ import annotations
 
