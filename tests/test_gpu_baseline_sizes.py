@@ -1,0 +1,85 @@
+"""CUDA device vs the CPU oracle at the sizes the benchmark runs (B200 only).
+
+These are the configurations ``bench.py`` times, so every timed code path has
+a correctness check at its timed size:
+
+* config 2, ``lnsm_8192_4096``: the row-fused LayerNorm+softmax kernel in its
+  staged schedule (persistent blocks, each walking ~28 rows through the
+  2-slot ``cp.async.bulk`` ring with mbarrier phase flips), and
+  ``lnsm_1000_4096``, whose row count does not divide the grid, so the last
+  blocks take the early-drain branch;
+* config 3, ``dotsig_4096``: the 4096^3 products on the tcgen05 path with the
+  planner's split-K and raster choices;
+* config 4, the full 4-layer batch-32 encoder proc after one SGD step, and a
+  4-layer encoder with the well-conditioned loss after three SGD steps.
+
+Tolerances are the ones of the reference comparison (reference test suite
+and BASELINE): rel 1e-4 / abs 1e-5 for fp32 outputs of one pass; rel 1e-3 for
+parameters after SGD steps.
+"""
+import numpy as np
+import pytest
+
+from tests.test_gpu_parity import both
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("case", ["lnsm_8192_4096", "lnsm_1000_4096"])
+def test_rowfused_staged_ring(case):
+    from ad_b200.device import CudaB200Device
+    from ad_b200.fixtures import load_case
+    p, _ = load_case(case)
+    rows = int(case.split("_")[1])
+    d = CudaB200Device()
+    d.prepare(p)
+    specs = [L.spec for ls in d.launches.values() for L in ls]
+    d.close()
+    # one kernel; a persistent grid smaller than the row count, so blocks loop
+    # over rows and the staging ring wraps
+    assert [s.kind for s in specs] == ["rowfused"]
+    assert specs[0].smem > 0 and specs[0].grid[0] < rows
+    got, want, _ = both(case)
+    for g, w in zip(got, want):
+        np.testing.assert_allclose(g, w, rtol=1e-4, atol=1e-5)
+
+
+def test_dotsig_4096():
+    """Config 3 at its benchmarked size: z, dX, dW, db against the oracle
+    (k-ordered fp32 dots) with the one-pass tolerance, and every dot output
+    against float64 with the 3xTF32 bound |C - C64| <= 1e-4 |A||B| + 1e-5."""
+    from ad_b200.fixtures import load_case
+    got, want, n = both("dotsig_4096", gemm="tc")
+    assert n > 0
+    for g, w in zip(got, want):
+        np.testing.assert_allclose(g, w, rtol=1e-4, atol=1e-5)
+    p, m = load_case("dotsig_4096")
+    arr = {c.id: np.asarray(c.content, np.float32) for c in p.procedure
+           if type(c).__name__ == "AllocEntry" and c.content is not None}
+    X = arr[m["X_id"]].reshape(4096, 4096).astype(np.float64)
+    W = arr[m["W_id"]].reshape(4096, 4096).astype(np.float64)
+    b = arr[m["b_id"]].astype(np.float64)
+    dz = arr[m["dz_id"]].reshape(4096, 4096).astype(np.float64)
+    z = 1.0 / (1.0 + np.exp(-(X @ W.T + b)))
+    np.testing.assert_allclose(got[0], z, rtol=1e-4, atol=1e-5)
+    dpre = dz * z * (1.0 - z)
+    dX = dpre @ W
+    bound = 1e-4 * (np.abs(dpre) @ np.abs(W)) + 1e-5
+    assert np.all(np.abs(got[1] - dX) <= bound)
+
+
+def test_encoder_4_layers_batch32_one_step():
+    """Config 4's own proc (4 layers, d512, 8 heads, ff2048, S128, batch 32):
+    every parameter after one SGD step, rel 1e-3."""
+    got, want, _ = both("enc_4_32_128_512_8_2048_100", loops=1)
+    assert len(got) == len(want) == 4 * (24 + 1 + 4 + 4)
+    for g, w in zip(got, want):
+        np.testing.assert_allclose(g, w, rtol=1e-3, atol=1e-4)
+
+
+def test_encoder_4_layers_three_steps():
+    """4 layers at config 4's layer shapes, batch 8, loss = sum(out * R) with a
+    fixed R ~ N(0,1): every parameter after three SGD steps, rel 1e-3."""
+    got, want, _ = both("encdy_4_8_128_512_8_2048_3", loops=3)
+    for g, w in zip(got, want):
+        np.testing.assert_allclose(g, w, rtol=1e-3, atol=1e-4)
