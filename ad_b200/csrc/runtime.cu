@@ -24,6 +24,7 @@
 #include <dlfcn.h>
 
 #include <chrono>
+#include <condition_variable>
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -179,6 +180,10 @@ struct ad_ctx {
   int rank = 0, world = 1;
   double nccl_timeout_s = 300.0;
   std::vector<char> last_log;
+  // pinned staging ring for copies from / to pageable host memory
+  std::vector<void*> stage;
+  std::vector<cudaEvent_t> stage_ev;
+  std::vector<bool> stage_busy;
 };
 
 struct ad_kernel {
@@ -201,6 +206,106 @@ static int stream_of(ad_ctx* c, int s, cudaStream_t* out) {
 
 static int set_dev(ad_ctx* c) {
   CK(cudaSetDevice(c->device));
+  return 0;
+}
+
+// ---------------------------------------------------------------- host copy pool
+// Copies between pageable and pinned host memory run on a few persistent
+// threads: one thread moves ~5-10 GB/s, the PCIe link ~50 GB/s per direction.
+class CopyPool {
+ public:
+  static CopyPool& get() {
+    static CopyPool pool;
+    return pool;
+  }
+  // dst[0, n) = src[0, n), split over the workers and the calling thread
+  void copy(void* dst, const void* src, size_t n) {
+    const size_t min_piece = 1 << 20;
+    size_t parts = n / min_piece;
+    if (parts > workers_.size() + 1) parts = workers_.size() + 1;
+    if (parts <= 1) {
+      memcpy(dst, src, n);
+      return;
+    }
+    size_t piece = ((n + parts - 1) / parts + 4095) & ~size_t(4095);
+    std::lock_guard<std::mutex> one_caller(call_m_);
+    std::unique_lock<std::mutex> lk(m_);
+    dst_ = static_cast<char*>(dst);
+    src_ = static_cast<const char*>(src);
+    n_ = n;
+    piece_ = piece;
+    next_ = 1;  // piece 0 is the caller's
+    pending_ = 0;
+    for (size_t i = 1; i < parts && i * piece < n; ++i) ++pending_;
+    ++gen_;
+    lk.unlock();
+    cv_.notify_all();
+    memcpy(dst, src, piece < n ? piece : n);
+    lk.lock();
+    done_cv_.wait(lk, [&] { return pending_ == 0; });
+  }
+
+ private:
+  CopyPool() {
+    unsigned hw = std::thread::hardware_concurrency();
+    unsigned nw = hw > 2 ? (hw / 2 < 8 ? hw / 2 : 8) - 1 : 0;
+    for (unsigned i = 0; i < nw; ++i) workers_.emplace_back([this] { run(); });
+  }
+  ~CopyPool() {
+    {
+      std::lock_guard<std::mutex> lk(m_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : workers_) t.join();
+  }
+  void run() {
+    uint64_t seen = 0;
+    std::unique_lock<std::mutex> lk(m_);
+    for (;;) {
+      cv_.wait(lk, [&] { return stop_ || (gen_ != seen && next_ * piece_ < n_ && pending_ > 0); });
+      if (stop_) return;
+      size_t i = next_++;
+      if (i * piece_ >= n_) {
+        seen = gen_;
+        continue;
+      }
+      char* d = dst_ + i * piece_;
+      const char* s = src_ + i * piece_;
+      size_t len = n_ - i * piece_ < piece_ ? n_ - i * piece_ : piece_;
+      lk.unlock();
+      memcpy(d, s, len);
+      lk.lock();
+      if (--pending_ == 0) {
+        seen = gen_;
+        done_cv_.notify_all();
+      }
+    }
+  }
+  std::vector<std::thread> workers_;
+  std::mutex call_m_, m_;
+  std::condition_variable cv_, done_cv_;
+  char* dst_ = nullptr;
+  const char* src_ = nullptr;
+  size_t n_ = 0, piece_ = 1, next_ = 0, pending_ = 0;
+  uint64_t gen_ = 0;
+  bool stop_ = false;
+};
+
+constexpr size_t kStageChunk = 8u << 20;  // bytes per staging slot
+constexpr int kStageSlots = 4;
+
+int ensure_stage(ad_ctx* c) {
+  if (!c->stage.empty()) return 0;
+  for (int i = 0; i < kStageSlots; ++i) {
+    void* p = nullptr;
+    cudaEvent_t e;
+    CK(cudaHostAlloc(&p, kStageChunk, cudaHostAllocPortable));
+    CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    c->stage.push_back(p);
+    c->stage_ev.push_back(e);
+    c->stage_busy.push_back(false);
+  }
   return 0;
 }
 
@@ -252,6 +357,9 @@ int ad_destroy(ad_ctx* c) {
   if (!c) return 0;
   cudaSetDevice(c->device);
   if (c->comm && g_nccl.ok) g_nccl.commDestroy(c->comm);
+  for (auto s : c->streams) cudaStreamSynchronize(s);
+  for (auto e : c->stage_ev) cudaEventDestroy(e);
+  for (auto p : c->stage) cudaFreeHost(p);
   for (auto s : c->streams) cudaStreamDestroy(s);
   delete c;
   return 0;
@@ -321,6 +429,56 @@ int ad_d2d(ad_ctx* c, uint64_t dst, uint64_t src, size_t bytes, int stream) {
   if (stream_of(c, stream, &s)) return 1;
   CK(cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), bytes,
                      cudaMemcpyDeviceToDevice, s));
+  return 0;
+}
+
+int ad_host_copy(void* dst, const void* src, size_t bytes) {
+  if (!bytes) return 0;
+  if (!dst || !src) return fail("ad_host_copy: null pointer");
+  CopyPool::get().copy(dst, src, bytes);
+  return 0;
+}
+
+int ad_h2d_pageable(ad_ctx* c, uint64_t dst, const void* src, size_t bytes, int stream) {
+  cudaStream_t s;
+  if (stream_of(c, stream, &s) || set_dev(c) || ensure_stage(c)) return 1;
+  const char* from = static_cast<const char*>(src);
+  for (size_t off = 0, i = 0; off < bytes; off += kStageChunk, ++i) {
+    int k = int(i % kStageSlots);
+    size_t len = bytes - off < kStageChunk ? bytes - off : kStageChunk;
+    if (c->stage_busy[k]) CK(cudaEventSynchronize(c->stage_ev[k]));  // its last copy has been read
+    CopyPool::get().copy(c->stage[k], from + off, len);
+    CK(cudaMemcpyAsync(reinterpret_cast<void*>(dst + off), c->stage[k], len, cudaMemcpyHostToDevice, s));
+    CK(cudaEventRecord(c->stage_ev[k], s));
+    c->stage_busy[k] = true;
+  }
+  return 0;
+}
+
+int ad_d2h_pageable(ad_ctx* c, void* dst, uint64_t src, size_t bytes, int stream) {
+  cudaStream_t s;
+  if (stream_of(c, stream, &s) || set_dev(c) || ensure_stage(c)) return 1;
+  char* to = static_cast<char*>(dst);
+  size_t n = (bytes + kStageChunk - 1) / kStageChunk;
+  auto issue = [&](size_t i) -> int {
+    int k = int(i % kStageSlots);
+    size_t off = i * kStageChunk, len = bytes - off < kStageChunk ? bytes - off : kStageChunk;
+    if (c->stage_busy[k]) CK(cudaEventSynchronize(c->stage_ev[k]));
+    CK(cudaMemcpyAsync(c->stage[k], reinterpret_cast<const void*>(src + off), len, cudaMemcpyDeviceToHost, s));
+    CK(cudaEventRecord(c->stage_ev[k], s));
+    c->stage_busy[k] = true;
+    return 0;
+  };
+  for (size_t i = 0; i < n && i < (size_t)kStageSlots; ++i)
+    if (issue(i)) return 1;
+  for (size_t i = 0; i < n; ++i) {
+    int k = int(i % kStageSlots);
+    size_t off = i * kStageChunk, len = bytes - off < kStageChunk ? bytes - off : kStageChunk;
+    CK(cudaEventSynchronize(c->stage_ev[k]));
+    c->stage_busy[k] = false;
+    CopyPool::get().copy(to + off, c->stage[k], len);
+    if (i + kStageSlots < n && issue(i + kStageSlots)) return 1;
+  }
   return 0;
 }
 

@@ -127,8 +127,8 @@ class CudaB200Device:
             if isinstance(c, ir.AllocEntry) and not c.is_temp and c.content is not None:
                 a = np.ascontiguousarray(np.asarray(c.content, dtype=np.float32).reshape(-1))
                 assert a.size <= c.size
-                self.ctx.h2d(self.ptr(c.id), a.ctypes.data, a.nbytes, 0)
-                self.ctx.sync(0)
+                self.ctx.h2d_pageable(self.ptr(c.id), a.ctypes.data, a.nbytes, 0)
+        self.ctx.sync(0)
 
     def upload(self, buf_id: int, arr: np.ndarray, offset: int = 0) -> None:
         a = np.ascontiguousarray(arr, dtype=np.float32)
@@ -279,16 +279,18 @@ class CudaB200Device:
             arr = cmd.func()
             assert isinstance(arr, np.ndarray) and list(arr.shape) == list(cmd.shape), "Invalid function"
             a = np.ascontiguousarray(arr, dtype=np.float32)
-            self.ctx.h2d(self.ptr(cmd.kres.id) + 4 * offset_of(cmd.kres), a.ctypes.data, a.nbytes, 0)
-            self.ctx.sync(0)  # the numpy array may be freed once we return
+            # staged through pinned memory; the array may be freed once this returns
+            self.ctx.h2d_pageable(self.ptr(cmd.kres.id) + 4 * offset_of(cmd.kres), a.ctypes.data, a.nbytes, 0)
             return
         if kind == "Receiver":
             outs = []
-            self.ctx.sync(0)
             for k in cmd.kargs:
                 n = math.prod(k.shape)
                 o = np.empty(n, dtype=np.float32)
-                self.ctx.d2h(o.ctypes.data, self.ptr(k.id) + 4 * offset_of(k), 4 * n, 0)
+                if 4 * n >= (1 << 20):
+                    self.ctx.d2h_pageable(o.ctypes.data, self.ptr(k.id) + 4 * offset_of(k), 4 * n, 0)
+                else:
+                    self.ctx.d2h(o.ctypes.data, self.ptr(k.id) + 4 * offset_of(k), 4 * n, 0)
                 outs.append(o)
             self.ctx.sync(0)
             outs = [o.reshape(k.shape) for o, k in zip(outs, cmd.kargs)]
@@ -386,7 +388,9 @@ class CudaB200Device:
                     for f in feeders:
                         arr = f.func()
                         assert isinstance(arr, np.ndarray) and list(arr.shape) == list(f.shape), "Invalid function"
-                        stagings[i][id(f)][:] = np.asarray(arr, dtype=np.float32).reshape(-1)
+                        a = np.ascontiguousarray(arr, dtype=np.float32)
+                        st = stagings[i][id(f)]
+                        rt.host_copy(st.ctypes.data, a.ctypes.data, min(a.nbytes, st.nbytes))
             g.launch(0)
             self.n_launches += n_kern * cu
             if feeders:

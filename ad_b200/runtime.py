@@ -39,6 +39,9 @@ SIGNATURES = {
     "ad_h2d": (c_int, [c_void_p, c_u64, c_void_p, c_size_t, c_int]),
     "ad_d2h": (c_int, [c_void_p, c_void_p, c_u64, c_size_t, c_int]),
     "ad_d2d": (c_int, [c_void_p, c_u64, c_u64, c_size_t, c_int]),
+    "ad_h2d_pageable": (c_int, [c_void_p, c_u64, c_void_p, c_size_t, c_int]),
+    "ad_d2h_pageable": (c_int, [c_void_p, c_void_p, c_u64, c_size_t, c_int]),
+    "ad_host_copy": (c_int, [c_void_p, c_void_p, c_size_t]),
     "ad_stream_sync": (c_int, [c_void_p, c_int]),
     "ad_sync": (c_int, [c_void_p]),
     "ad_event_create": (c_int, [c_void_p, c_int, ctypes.POINTER(c_void_p)]),
@@ -145,6 +148,11 @@ def compile_cubin(src: str, name: str = "k.cu", opts: Optional[Sequence[str]] = 
 
 # ------------------------------------------------------------------ context wrapper
 
+def host_copy(dst_ptr: int, src_ptr: int, nbytes: int) -> None:
+    """memcpy on the library's copy threads."""
+    check(lib().ad_host_copy(dst_ptr, src_ptr, nbytes), "ad_host_copy")
+
+
 class Context:
     """One device context: streams, memory, kernels (C-ABI ``ad_ctx``)."""
 
@@ -186,6 +194,14 @@ class Context:
 
     def d2h(self, dst_ptr: int, src: int, nbytes: int, stream: int = 0) -> None:
         check(self.L.ad_d2h(self.h, dst_ptr, src, nbytes, stream), "ad_d2h")
+
+    def h2d_pageable(self, dst: int, src_ptr: int, nbytes: int, stream: int = 0) -> None:
+        """From pageable host memory; ``src`` may be reused on return."""
+        check(self.L.ad_h2d_pageable(self.h, dst, src_ptr, nbytes, stream), "ad_h2d_pageable")
+
+    def d2h_pageable(self, dst_ptr: int, src: int, nbytes: int, stream: int = 0) -> None:
+        """Into pageable host memory; complete on return."""
+        check(self.L.ad_d2h_pageable(self.h, dst_ptr, src, nbytes, stream), "ad_d2h_pageable")
 
     def d2d(self, dst: int, src: int, nbytes: int, stream: int = 0) -> None:
         check(self.L.ad_d2d(self.h, dst, src, nbytes, stream), "ad_d2d")

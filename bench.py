@@ -1,21 +1,32 @@
 """Benchmark of the B200 device backend on BASELINE.json's configurations.
 
-Default (N=1): config 2, the fused Reduce+elementwise microbench --
-LayerNorm then softmax over the last dim of fp32 [8192, 4096], forward plus
-backward w.r.t. x -- run as the proc the reference front-end produces for it
-(tests/golden/procs/lnsm_8192_4096.json.gz).  One step = one pass of every
-compute command of that proc over inputs already resident in HBM.
+Default: the transformer-encoder training step of config 4 (4 layers, d512,
+8 heads, ff2048, S128, batch 32, fp32, SGD), run as the proc the reference
+front-end produces for it (tests/golden/procs/enc_4_32_128_512_8_2048_100).
+One step = one iteration of the proc's training loop (Feeder copy of the
+batch, forward, backward, SGD update), replayed as CUDA graphs.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload lnsm|dotsig|mlp]
+* N=1: config 4 itself.
+* N>1 (torchrun, one rank per GPU): data parallel, weak scaling -- every rank
+  runs the batch-32 step on its own inputs and the NCCL all-reduce of the
+  gradients before each SGD update (``ad_b200.dist``) makes it one global step
+  of 32*N sequences.  ``value`` is sequences/s of the whole job, device-timed
+  (CUDA events), max over ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
     python bench.py --impl reference ...   # the reference's kernels on the host CPU
 
-``value`` = fused-kernel HBM throughput: sum over the step's kernels of their
-algorithmic bytes (unique extents read + written) / step time.  ``e2e`` =
-the same bytes through the public device API with host-resident inputs:
-pinned host->device copy of x and dy, the step, device->host copy of y and dx.
-Multi-GPU (torchrun): every rank runs its own replica ("weak" scaling, no
-data-path collective; the LayerNorm/softmax rows are independent), barrier +
-CUDA-event timing, max over ranks.
+Other workloads: ``lnsm`` (config 2, LayerNorm+softmax fwd+bwd, fused-kernel
+HBM GB/s), ``dotsig`` (config 3, TFLOP/s), ``mlp`` (config 1), ``enc12``
+(config 5's per-GPU shard: 12 layers, d1024, 16 heads, ff4096, S512, batch 32
+per GPU; at 8 GPUs it is config 5's global batch of 256), ``enc3_d1024``,
+``enc`` (strong scaling of config 4's global batch of 32), ``enc_small``.
+
+``e2e`` is the same metric through the device's public run pass with host
+data: the Feeder's ``func()`` returns a pageable numpy array each step, the
+device stages and copies it, and the Receiver hands freshly allocated numpy
+arrays to its callback (host wall clock around the whole call, after a device
+synchronize on both sides).
 """
 import argparse
 import json
@@ -44,9 +55,13 @@ WORKLOADS = {
             "unit": "steps/s", "loop": True, "cpu_iters": 1, "dp": True, "global_batch": 32,
             "data": "synthetic: x ~ N(0,1) [4096, 512] seed 0 via Feeder; Xavier-uniform weights (seeded)"},
     "enc_weak": {"case": "enc_4_32_128_512_8_2048_100",
-                 "metric": "encoder train sequences/s (4 layers, d512, 8 heads, ff2048, S128, batch 32 per GPU, fp32, SGD)",
+                 "metric": "encoder train sequences/s (config 4: 4 layers, d512, 8 heads, ff2048, S128, batch 32 per GPU, fp32, SGD; data parallel over N GPUs)",
                  "unit": "sequences/s", "loop": True, "cpu_iters": 1, "dp": "weak", "batch_per_gpu": 32,
                  "data": "synthetic: x ~ N(0,1) [4096, 512] per rank (seed 1000*rank) via Feeder; Xavier-uniform weights (seeded, same on every rank)"},
+    "enc12": {"case": "enc_12_256_512_1024_16_4096_50_p8",
+              "metric": "encoder train sequences/s (config 5 shard: 12 layers, d1024, 16 heads, ff4096, S512, batch 32 per GPU, fp32, SGD; data parallel over N GPUs)",
+              "unit": "sequences/s", "loop": True, "cpu_iters": 0, "dp": "weak", "batch_per_gpu": 32,
+              "data": "synthetic: x ~ N(0,1) [32*512, 1024] per rank (seed 1000*rank) via Feeder; Xavier-uniform weights (seeded, same on every rank)"},
     "enc3_d1024": {"case": "enc_3_96_512_1024_16_4096_50_p3",
                    "metric": "encoder train sequences/s (3 layers, d1024, 16 heads, ff4096, S512, batch 32 per GPU, fp32, SGD)",
                    "unit": "sequences/s", "loop": True, "cpu_iters": 0, "dp": "weak", "batch_per_gpu": 32,
@@ -223,6 +238,23 @@ def cpu_reference(args, wl, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def feeder_proc(proc, dev, in_ids):
+    """The prepared ``proc`` with its input buffers fed by Feeders (placed
+    before the first command) whose ``func()`` returns a pageable numpy array,
+    as a user of ``execute()`` supplies data.  Returns (proc, h2d, d2h bytes)."""
+    from ad_b200 import ir
+    feeders, h2d = [], 0
+    for i, b in enumerate(in_ids):
+        n = dev.slots[b].size
+        arr = np.random.default_rng(100 + i).standard_normal(n, dtype=np.float32)
+        k = ir.KMatrix(b, ir.Gid(), [n])
+        feeders.append(ir.Feeder(-1 - i, [n], k, f"in{i}", func=lambda a=arr: a))
+        h2d += arr.nbytes
+    recv = [c for c in proc.procedure if type(c).__name__ == "Receiver"]
+    d2h = sum(4 * int(np.prod(k.shape)) for r in recv for k in r.kargs)
+    return ir.Proc(feeders + list(proc.procedure)), h2d, d2h
+
+
 def alg_bytes_of(p):
     from ad_b200 import codegen, ir, memplan
     slots, _ = memplan.plan(p)
@@ -246,18 +278,22 @@ def step_value(wl, alg_bytes, seconds):
     return wl["flops"] / seconds / 1e12
 
 
-def main():
+def build_parser():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="lnsm", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="enc_weak", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-timing", action="store_true",
                     help="skip the per-kernel isolated timings (loop workloads)")
-    args = ap.parse_args()
+    return ap
+
+
+def main():
+    args = build_parser().parse_args()
     args.warmup = max(args.warmup, 3)
     wl = WORKLOADS[args.workload]
     rank, world, local = dist_env()
@@ -342,37 +378,25 @@ def main():
     roof.update({"kernel": f"{top}:{Lt.spec.kind}", "kernel_ms": float(per_kernel[top]),
                  "alg_bytes": Lt.spec.bytes_moved, "traffic_source": traffic_src})
 
-    # e2e through the public API with host-resident inputs (pinned)
+    # e2e through the device's public run pass: the inputs enter as Feeders
+    # whose func() returns pageable numpy arrays, the proc's Receiver hands
+    # fresh numpy arrays to its callback
     in_ids = [meta[k] for k in wl.get("inputs", ("x_id", "dy_id")) if k in meta]
-    recv = [c for c in proc.procedure if type(c).__name__ == "Receiver"]
-    out_refs = [(k.id, int(np.prod(k.shape))) for r in recv for k in r.kargs]
-    host_in = {}
-    for b in in_ids:
-        a = dev._pinned(4 * dev.slots[b].size)
-        a[:] = 0.5
-        host_in[b] = a
-    host_out = [dev._pinned(4 * n) for _, n in out_refs]
+    fproc, h2d, d2h = feeder_proc(proc, dev, in_ids)
     e2e_steps = max(3, args.steps // 2)
-
-    def e2e_step():
-        for b, a in host_in.items():
-            ctx.h2d(dev.ptr(b), a.ctypes.data, a.nbytes, 0)
-        step_graph.launch(0)
-        for (b, n), o in zip(out_refs, host_out):
-            ctx.d2h(o.ctypes.data, dev.ptr(b), 4 * n, 0)
-
-    e2e_step()
+    got = []
+    for c in fproc.procedure:
+        if type(c).__name__ == "Receiver":
+            c.func = lambda *outs: got.append(len(outs))
+    dev._run_proc(fproc, dev.run)
     ctx.sync()
     barrier(td)
-    e0, e1 = ctx.event(True), ctx.event(True)
-    e0.record(0)
+    t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(0)
-    e1.sync()
-    e2e_ms = allmax(td, e0.elapsed_ms(e1) / e2e_steps)
-    h2d = sum(a.nbytes for a in host_in.values())
-    d2h = sum(o.nbytes for o in host_out)
+        dev._run_proc(fproc, dev.run)
+    ctx.sync()
+    e2e_ms = allmax(td, (time.perf_counter() - t0) * 1e3 / e2e_steps)
+    assert len(got) == e2e_steps + 1
 
     if rank == 0:
         line = {
@@ -392,7 +416,10 @@ def main():
             "per_kernel_GBps": [round(L.spec.bytes_moved / (t / 1e3) / 1e9, 1) for L, t in zip(launches, per_kernel)],
             "clocks": clk.summary(),
             "e2e": {"value": step_value(wl, wl.get("min_bytes", alg_bytes), e2e_ms / 1e3) * world, "unit": wl["unit"],
-                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "note": "per step one call of the device's run pass: Feeders of the inputs (pageable "
+                            "numpy arrays), the step's kernels, the Receiver's copies into fresh numpy "
+                            "arrays and its callback; host wall clock"},
             "compile_s": round(dev.compile_seconds, 2),
         }
         if not args.no_cpu_baseline:
@@ -418,6 +445,9 @@ def bench_loop(args, wl, rank, world, local, td):
         if not weak:
             case = f"{case}_p{world}"
         from ad_b200 import dist
+        # NCCL's init lines name the communicator's rank count (and NVLS use)
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         box = [dist.nccl_unique_id() if rank == 0 else None]
         td.broadcast_object_list(box, src=0)
         dp = (rank, world, box[0])
@@ -478,6 +508,7 @@ def bench_loop(args, wl, rank, world, local, td):
     l2_note = (f"step working set {work_set / 1e6:.0f} MB (arena + dot-operand scratch) "
                + ("exceeds the 126 MB L2" if work_set > 126e6 else "fits in the 126 MB L2 (small model)"))
     feed_bytes = sum(4 * int(np.prod(c.shape)) for c in ir.iter_cmds(loop.proc) if type(c).__name__ == "Feeder")
+    e2e = e2e_loop(dev, proc, loop, args.steps, td)
     if weak:
         value = 1e3 / ms * wl["batch_per_gpu"] * world       # sequences per second, whole job
     else:
@@ -501,16 +532,52 @@ def bench_loop(args, wl, rank, world, local, td):
             "per_kernel_GBps": [round(L.spec.bytes_moved / (t / 1e3) / 1e9, 1) if t > 0 else None
                                 for L, t in zip(launches, per_kernel)],
             "clocks": clk.summary(),
-            "e2e": {"value": value, "unit": wl["unit"], "h2d_bytes_per_step": feed_bytes,
-                    "d2h_bytes_per_step": 0,
-                    "note": "the timed loop calls the Feeder and copies its batch host-to-device every step; "
-                            "the proc reads parameters back once after the loop (Receiver)"},
+            "e2e": {"value": (value * ms / e2e["ms_per_step"]), "unit": wl["unit"],
+                    "ms_per_step": e2e["ms_per_step"], "h2d_bytes_per_step": feed_bytes,
+                    "d2h_bytes_per_step": e2e["d2h_bytes"] / args.steps,
+                    "note": "one call of the device's run pass over the proc with the loop set to the timed "
+                            "step count: each step calls the Feeder (a pageable numpy batch), which the device "
+                            "stages into pinned memory and copies inside the step's graph; after the loop the "
+                            "Receiver copies every parameter back into fresh numpy arrays and calls its "
+                            "callback (d2h bytes amortised over the steps); host wall clock, max over ranks"},
         }
-        if not args.no_cpu_baseline and wl["cpu_iters"] > 0:
+        if not args.no_cpu_baseline and wl["cpu_iters"] > 0 and world == 1:
             line["cpu_baseline"] = cpu_loop_baseline(wl)
         print(json.dumps(line), flush=True)
     dev.close()
     barrier(td)
+
+
+def e2e_loop(dev, proc, loop, steps, td):
+    """The public run pass (``CudaB200Device._run_proc`` with ``run``, as
+    ``execute`` calls it after init) over ``steps`` loop iterations, with the
+    Feeder returning pageable numpy arrays; host wall clock."""
+    import time as _t
+    from ad_b200 import ir
+    feeders = [c for c in ir.iter_cmds(loop.proc) if type(c).__name__ == "Feeder"]
+    saved = [(f, f.func) for f in feeders]
+    for f, fn in saved:
+        first = np.array(fn(), dtype=np.float32, copy=True)
+        pool = [first, first[::-1].copy()]          # two distinct pageable host arrays
+        cnt = [0]
+
+        def feed(pool=pool, cnt=cnt):
+            cnt[0] += 1
+            return pool[cnt[0] % 2]
+        f.func = feed
+    recv = [c for c in ir.iter_cmds(proc) if type(c).__name__ == "Receiver"]
+    d2h = sum(4 * int(np.prod(k.shape)) for r in recv for k in r.kargs)
+    loop.r = range(steps)
+    dev._run_proc(proc, dev.run)             # graphs for this loop length exist after the first call
+    dev.ctx.sync()
+    barrier(td)
+    t0 = _t.perf_counter()
+    dev._run_proc(proc, dev.run)
+    dev.ctx.sync()
+    dt = allmax(td, _t.perf_counter() - t0)
+    for f, fn in saved:
+        f.func = fn
+    return {"ms_per_step": dt * 1e3 / steps, "d2h_bytes": d2h}
 
 
 def cpu_loop_baseline(wl):

@@ -57,6 +57,17 @@ int ad_h2d(ad_ctx* ctx, uint64_t dst, const void* src, size_t bytes, int stream)
 /* cl_helper.py:262-302 read_buffers; cuda_helper.py:86-111 (cuMemcpyDtoH) */
 int ad_d2h(ad_ctx* ctx, void* dst, uint64_t src, size_t bytes, int stream);
 int ad_d2d(ad_ctx* ctx, uint64_t dst, uint64_t src, size_t bytes, int stream);
+/* cl_helper.py:304-332 write_buffer / cuda_helper.py:113-126 with the numpy
+ * array's own (pageable) memory as source: staged through a ring of pinned
+ * buffers, host copies on a few threads overlapped with the DMA.  Returns once
+ * `src` may be reused; the device copy completes in stream order. */
+int ad_h2d_pageable(ad_ctx* ctx, uint64_t dst, const void* src, size_t bytes, int stream);
+/* cl_helper.py:262-302 read_buffers / cuda_helper.py:86-111 into a pageable
+ * (freshly allocated numpy) destination; returns when `dst` holds the data. */
+int ad_d2h_pageable(ad_ctx* ctx, void* dst, uint64_t src, size_t bytes, int stream);
+/* Host memcpy on the library's copy threads (numpy -> pinned Feeder staging;
+ * the reference copies with numpy, cl_helper.py:318-322). */
+int ad_host_copy(void* dst, const void* src, size_t bytes);
 /* cl_helper.py:457 waitAll (clFinish) */
 int ad_stream_sync(ad_ctx* ctx, int stream);
 int ad_sync(ad_ctx* ctx);

@@ -37,6 +37,7 @@ reduce sizes, where the reference tree drops elements).
 from __future__ import annotations
 
 import ctypes
+import re
 import hashlib
 import math
 import os
@@ -296,7 +297,13 @@ class OracleDevice:
     """CPU executor with the reference device's walk (opencl/device.py:46-130)."""
 
     def __init__(self, faithful_tree: bool = True, threads: Optional[int] = None,
-                 dot_rows: Optional[int] = None):
+                 dot_rows: Optional[int] = None, f64: bool = False):
+        """``f64=True``: the same kernels with every float (buffers, temporaries,
+        accumulators) widened to double -- a near-exact value of what the
+        reference computes, used to judge rounding differences between two fp32
+        results (never as the checked result itself)."""
+        self.f64 = f64
+        self.dtype = np.float64 if f64 else np.float32
         self.faithful_tree = faithful_tree
         self.dot_rows = dot_rows
         self.buffers: Dict[int, np.ndarray] = {}
@@ -315,7 +322,7 @@ class OracleDevice:
             if isinstance(c, ir.AllocEntry) and not c.is_temp and getattr(c, "alias", None):
                 aliases.append(c)
             elif isinstance(c, ir.AllocEntry) and not c.is_temp:
-                buf = np.zeros(c.size, dtype=np.float32)
+                buf = np.zeros(c.size, dtype=self.dtype)
                 if c.content is not None:
                     buf[:] = np.asarray(c.content, dtype=np.float32).reshape(-1)
                 self.buffers[c.id] = buf
@@ -326,6 +333,8 @@ class OracleDevice:
         for c in aliases:   # views into another buffer (ad_b200.dist gradient slices)
             base, off = c.alias
             self.buffers[c.id] = self.buffers[base][off:off + c.size]
+        if self.f64:
+            srcs = {k: re.sub(r"\bfloat\b", "double", v) for k, v in srcs.items()}
         lib = compile_kernels(srcs) if srcs else None
         for c, name in self._cmds:
             fn = getattr(lib, name)

@@ -33,3 +33,15 @@ def test_version_and_errors_without_gpu():
 def test_nvrtc_compiles_sm100a():
     cub = rt.compile_cubin('extern "C" __global__ void k(float* p) { p[threadIdx.x] = 1.0f; }', "t.cu")
     assert len(cub) > 100
+
+
+def test_host_copy_threads():
+    """ad_host_copy (the Feeder staging copy) on sizes around its split points."""
+    import numpy as np
+    from ad_b200 import runtime as rt
+    rng = np.random.default_rng(3)
+    for n in (0, 1, 4095, 1 << 20, (1 << 20) + 3, (7 << 20) + 12345, 33 << 20):
+        src = rng.integers(0, 255, n, dtype=np.uint8)
+        dst = np.zeros(n + 16, np.uint8)
+        rt.host_copy(dst.ctypes.data, src.ctypes.data, n)
+        assert np.array_equal(dst[:n], src) and not dst[n:].any()

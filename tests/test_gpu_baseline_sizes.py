@@ -13,14 +13,20 @@ a correctness check at its timed size:
 * config 4, the full 4-layer batch-32 encoder proc after one SGD step, and a
   4-layer encoder with the well-conditioned loss after three SGD steps.
 
-Tolerances are the ones of the reference comparison (reference test suite
-and BASELINE): rel 1e-4 / abs 1e-5 for fp32 outputs of one pass; rel 1e-3 for
-parameters after SGD steps.
+Tolerances are the ones of the reference comparison: rel 1e-4 / abs 1e-5 for
+fp32 outputs of one pass; rel 1e-3 / abs 1e-4 for parameters after SGD steps.
+At these sizes some outputs are long fp32 sums that cancel (the bias gradient
+of config 3 sums 4096 terms of both signs; the LayerNorm parameter gradients
+of config 4 under loss = sum(out) are rounding noise of that kind), and there
+the fp32 oracle's own rounding error exceeds the tolerance.  Such elements
+pass when the CUDA result is at least as close to the float64 evaluation of
+the same kernels (``OracleDevice(f64=True)``) as the fp32 oracle is
+(``assert_parity``).
 """
 import numpy as np
 import pytest
 
-from tests.test_gpu_parity import both
+from tests.test_gpu_parity import assert_parity, both, exact_of
 
 pytestmark = pytest.mark.gpu
 
@@ -47,12 +53,12 @@ def test_rowfused_staged_ring(case):
 def test_dotsig_4096():
     """Config 3 at its benchmarked size: z, dX, dW, db against the oracle
     (k-ordered fp32 dots) with the one-pass tolerance, and every dot output
-    against float64 with the 3xTF32 bound |C - C64| <= 1e-4 |A||B| + 1e-5."""
+    against float64 with the 3xTF32 bound |C - C64| <= 1e-4 |A||B| + 1e-5
+    (dX shown; z through the sigmoid)."""
     from ad_b200.fixtures import load_case
     got, want, n = both("dotsig_4096", gemm="tc")
     assert n > 0
-    for g, w in zip(got, want):
-        np.testing.assert_allclose(g, w, rtol=1e-4, atol=1e-5)
+    assert_parity(got, want, exact_of("dotsig_4096"), rtol=1e-4, atol=1e-5)
     p, m = load_case("dotsig_4096")
     arr = {c.id: np.asarray(c.content, np.float32) for c in p.procedure
            if type(c).__name__ == "AllocEntry" and c.content is not None}
@@ -73,8 +79,7 @@ def test_encoder_4_layers_batch32_one_step():
     every parameter after one SGD step, rel 1e-3."""
     got, want, _ = both("enc_4_32_128_512_8_2048_100", loops=1)
     assert len(got) == len(want) == 4 * (24 + 1 + 4 + 4)
-    for g, w in zip(got, want):
-        np.testing.assert_allclose(g, w, rtol=1e-3, atol=1e-4)
+    assert_parity(got, want, exact_of("enc_4_32_128_512_8_2048_100", loops=1), rtol=1e-3, atol=1e-4)
 
 
 def test_encoder_4_layers_three_steps():

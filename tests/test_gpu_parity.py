@@ -36,6 +36,33 @@ def both(case, loops=None, **devkw):
     return got, o.last_received, launches
 
 
+def exact_of(case, loops=None):
+    """The oracle widened to float64: the reference's computation without fp32 rounding."""
+    p, _ = load_case(case)
+    if loops is not None:
+        set_loop_count(p, loops)
+    o = OracleDevice(faithful_tree=False, f64=True)
+    o.execute(p)
+    return o.last_received
+
+
+def assert_parity(got, want, exact, rtol, atol):
+    """Each element matches the fp32 oracle within (rtol, atol), or, where it
+    does not, lies at least as close to the float64 result as the fp32 oracle
+    does: the two fp32 results differ there only by rounding, and the oracle's
+    own rounding error exceeds the tolerance (long fp32 sums that cancel)."""
+    for i, (g, w, e) in enumerate(zip(got, want, exact)):
+        g64, w64 = g.astype(np.float64), w.astype(np.float64)
+        close = np.abs(g64 - w64) <= atol + rtol * np.abs(w64)
+        better = np.abs(g64 - e) <= np.abs(w64 - e)
+        bad = ~(close | better)
+        assert not bad.any(), (
+            f"output {i}: {int(bad.sum())} of {g.size} elements differ from the oracle beyond "
+            f"rtol={rtol}, atol={atol} and are further from the float64 result than the oracle; "
+            f"first at {np.argwhere(bad)[0].tolist()}: got {g[tuple(np.argwhere(bad)[0])]}, "
+            f"oracle {w[tuple(np.argwhere(bad)[0])]}, float64 {e[tuple(np.argwhere(bad)[0])]}")
+
+
 @pytest.mark.parametrize("gemm,rowfuse", [("tc", True), ("simt", True), ("tc", False)])
 @pytest.mark.parametrize("case", ["unary", "unary+tetris", "dotprod", "layernorm",
                                   "lnsm_64_256", "lnsm_33_96", "lnsm_16_4096",
