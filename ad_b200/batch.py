@@ -119,6 +119,9 @@ def _levels(cmds: List, signature) -> List[int]:
     for i in range(n - 1, -1, -1):
         for j in succs[i]:
             hi[i] = min(hi[i], hi[j] - 1)
+    # commands marked ``late`` (joins of asynchronous collectives) go as late as
+    # their successors allow, so the work between fork and join overlaps
+    late = [i for i, c in enumerate(cmds) if getattr(c, "late", False)]
     sigs = [signature(c) for c in cmds]
     classes: Dict[str, List[int]] = {}
     for i, sg in enumerate(sigs):
@@ -141,6 +144,11 @@ def _levels(cmds: List, signature) -> List[int]:
                 if hi[j] > hi[i] - 1:
                     hi[j] = hi[i] - 1
                     work.append(j)
+
+    for i in late:
+        lo[i] = hi[i]
+        fixed[i] = True
+    narrow(late)
 
     while True:
         best = (1, None, None)

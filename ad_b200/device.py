@@ -42,6 +42,7 @@ from . import runtime as rt
 ELEMENTWISE = ("ElwFuse", "BinaryNode", "UnaryNode", "ContigiousNode")
 REDUCE = ("ReduceNode", "ReduceElwFuse")
 DOT = ("DotProdNode", "DPElwFuse")
+COMM_STREAM = 3          # the context's communication stream (include/ad_b200.h)
 
 
 _KERNEL_OPEN = re.compile(r'(extern "C" __global__ void [^{]*\{)')
@@ -113,6 +114,11 @@ class CudaB200Device:
         self.n_launches = 0
         self.compile_seconds = 0.0
         self.proc: Optional[ir.Proc] = None
+        # diagnostics: per all-reduce (bytes, async, start event, end event) when
+        # a list; AD_DP_SKIP_COMM=1 leaves the collectives out (timing only:
+        # ranks then diverge)
+        self.comm_trace = None
+        self.skip_comm = os.environ.get("AD_DP_SKIP_COMM", "0") == "1"
 
     # ------------------------------------------------------------ memory
     def ptr(self, buf_id: int) -> int:
@@ -224,7 +230,12 @@ class CudaB200Device:
                 if off < 0 or off + n > self.slots[k.id].size:
                     raise ValueError(f"{kind} access out of range for buffer {k.id}")
             return
-        if kind in ("AllocEntry", "DeallocEntry", "ForNode", "AllReduce"):
+        if kind == "AllReduce" and cmd.async_start:
+            # fork/join events of the communication stream (recorded again by
+            # every replay; inside a graph capture they become dependencies)
+            self._comm_events[id(cmd)] = (self.ctx.event(False), self.ctx.event(False))
+            return
+        if kind in ("AllocEntry", "DeallocEntry", "ForNode", "AllReduce", "AllReduceWait"):
             return
         self._pending.append((cmd, self._specs_for(cmd)))
 
@@ -300,7 +311,27 @@ class CudaB200Device:
             return
         if kind == "AllReduce":
             p = self.ptr(cmd.buf) + 4 * cmd.offset
-            rt.check(self.ctx.L.ad_allreduce_f32(self.ctx.h, p, p, cmd.count, 0, 0), "ad_allreduce_f32")
+            stream = COMM_STREAM if cmd.async_start else 0
+            if cmd.async_start:
+                fork, join = self._comm_events[id(cmd)]
+                fork.record(0)
+                fork.wait_on(COMM_STREAM)
+            trace = self.comm_trace
+            if trace is not None:
+                t0, t1 = self.ctx.event(True), self.ctx.event(True)
+                t0.record(stream)
+            if not self.skip_comm:
+                rt.check(self.ctx.L.ad_allreduce_f32(self.ctx.h, p, p, cmd.count, 0, stream),
+                         "ad_allreduce_f32")
+            if trace is not None:
+                t1.record(stream)
+                trace.append((cmd.count * 4, cmd.async_start, t0, t1))
+            if cmd.async_start:
+                join.record(COMM_STREAM)
+            return
+        if kind == "AllReduceWait":
+            for st in cmd.starts:
+                self._comm_events[id(st)][1].wait_on(0)
             return
         for L in self.launches[id(cmd)]:
             self._launch(L)
@@ -410,6 +441,7 @@ class CudaB200Device:
         from . import gemm
         gemm.setup_scratch(self, proc)
         self._pending = []
+        self._comm_events = {}
         self._run_proc(proc, self.init, init=True)
         self._compile_pending()
         return proc

@@ -14,10 +14,13 @@ of the global batch) so that
    bucket ``GB`` (``g_W[G] = T + 0``; ``g_W`` is a buffer aliased to
    ``GB[off_W:]``, so that independent gradient kernels stay independent for
    scheduling while the all-reduce sees one contiguous range);
-2. pending slices are flushed -- ``AllReduce`` (sum over ranks) of their
-   contiguous range of ``GB``, then one update per parameter,
-   ``W[G] = W[G] + g_W[G]`` -- right before the first later command
-   that reads one of those parameters, and at the end of the loop body.
+2. finished slices are summed over ranks in buckets: once the pending
+   slices reach ``AD_DP_BUCKET_MB`` (8 MiB), an ``AllReduce`` of their
+   contiguous range of ``GB`` starts on the device's communication stream
+   while the backward pass goes on; an ``AllReduceWait``, placed as late as
+   possible, joins it back, and then one update per parameter,
+   ``W[G] = W[G] + g_W[G]``, runs -- before the first later command that reads
+   one of those parameters, else at the end of the loop body.
 
 The loss is a sum over examples, so the summed ``-lr * grad`` of the shards
 equals the full-batch update: no division by the world size.  Flushing before
@@ -31,6 +34,7 @@ readers all parameters share one all-reduce at the end of the step.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Tuple
 
@@ -48,17 +52,37 @@ def _fresh_id() -> int:
 class AllReduce:
     """Sum ``count`` floats of buffer ``buf`` starting at element ``offset`` over
     all ranks, in place.  ``members`` are the per-parameter slice buffers
-    (aliases into ``buf``) the range covers, for dependency tracking."""
+    (aliases into ``buf``) the range covers, for dependency tracking.  With
+    ``async_start`` the device runs it on its communication stream, forked from
+    the compute stream at this point; an ``AllReduceWait`` joins it back."""
     buf: int
     count: int
     offset: int = 0
     members: Tuple[int, ...] = ()
     program_id: int = -1
     comm: object = None
+    async_start: bool = False
 
     def accesses(self) -> Tuple[List[int], List[int]]:
         ids = list(self.members) or [self.buf]
         return ids, ids
+
+
+@dataclass
+class AllReduceWait:
+    """The compute stream waits for the all-reduces ``starts``.  Scheduled as
+    late as its successors allow (``late``), so the reduction overlaps the
+    compute between its start and the first command that needs its result."""
+    starts: List[AllReduce]
+    program_id: int = -1
+    late: bool = True
+
+    def accesses(self) -> Tuple[List[int], List[int]]:
+        ids = [m for s in self.starts for m in (list(s.members) or [s.buf])]
+        return ids, ids
+
+
+BUCKET_BYTES = int(float(os.environ.get("AD_DP_BUCKET_MB", "8")) * (1 << 20))
 
 
 def _is_update(n, content_ids) -> bool:
@@ -69,14 +93,16 @@ def _is_update(n, content_ids) -> bool:
             and isinstance(n.kargs[0].access, ir.Gid))
 
 
-def insert_grad_allreduce(proc: ir.Proc, comm=None) -> Optional[int]:
+def insert_grad_allreduce(proc: ir.Proc, comm=None, bucket_bytes: Optional[int] = None) -> Optional[int]:
     """Rewrite ``proc`` in place (see module docstring).  Returns the bucket's
-    buffer id, or None when the proc has no in-place parameter update."""
+    buffer id of the last rewritten body, or None when the proc has no in-place
+    parameter update.  Loop bodies and the top level are rewritten alike."""
     from .memplan import _accesses
+    cap = BUCKET_BYTES if bucket_bytes is None else bucket_bytes
     content = {c.id: c.size for c in ir.iter_cmds(proc)
                if isinstance(c, ir.AllocEntry) and c.content is not None}
     loops = [c for c in proc.procedure if isinstance(c, ir.ForNode)]
-    bodies = [l.proc for l in loops] or [proc]
+    bodies = [l.proc for l in loops] + [proc]
     gb = None
     for body in bodies:
         has = any(_is_update(n, content) for c in body.procedure
@@ -85,38 +111,58 @@ def insert_grad_allreduce(proc: ir.Proc, comm=None) -> Optional[int]:
             continue
         gb = _fresh_id()
         total = 0
-        pending: List[Tuple[int, int, int, int]] = []     # (param, offset, n_el, slice id)
+        pending: List[Tuple[int, int, int, int]] = []     # (param, offset, n_el, slice id): not started
+        inflight: List[Tuple[AllReduce, list]] = []        # started, updates not applied
         new_body: List = []
         slices: List[ir.AllocEntry] = []
 
-        def flush():
+        def start(async_start: bool):
             nonlocal pending
             if not pending:
                 return
             start_off = pending[0][1]
             end_off = pending[-1][1] + (pending[-1][2] + 63) // 64 * 64
-            new_body.append(AllReduce(gb, end_off - start_off, start_off,
-                                      tuple(sid for _, _, _, sid in pending), comm=comm))
-            for w, off, n_el, sid in pending:
-                new_body.append(ir.BinaryNode(_fresh_id(), "ADD",
-                                              [ir.KMatrix(w, ir.Gid(), [n_el]), ir.KMatrix(sid, ir.Gid(), [n_el])],
-                                              ir.KMatrix(w, ir.Gid(), [n_el]), [n_el], True))
+            ar = AllReduce(gb, end_off - start_off, start_off,
+                           tuple(sid for _, _, _, sid in pending), comm=comm, async_start=async_start)
+            new_body.append(ar)
+            inflight.append((ar, pending))
             pending = []
+
+        def finish(which):
+            """Wait for the started buckets ``which`` and apply their updates."""
+            nonlocal inflight
+            if not which:
+                return
+            asyncs = [ar for ar, _ in which if ar.async_start]
+            if asyncs:
+                new_body.append(AllReduceWait(asyncs))
+            for _, members in which:
+                for w, off, n_el, sid in members:
+                    new_body.append(ir.BinaryNode(_fresh_id(), "ADD",
+                                                  [ir.KMatrix(w, ir.Gid(), [n_el]), ir.KMatrix(sid, ir.Gid(), [n_el])],
+                                                  ir.KMatrix(w, ir.Gid(), [n_el]), [n_el], True))
+            inflight = [x for x in inflight if all(x is not y for y in which)]
+
+        def need(params):
+            """Every update of ``params`` must be applied before the next command."""
+            if any(w in params for w, _, _, _ in pending):
+                start(True)
+            finish([x for x in inflight if any(w in params for w, _, _, _ in x[1])])
 
         for c in body.procedure:
             kind = type(c).__name__
-            if kind not in ("AllocEntry", "DeallocEntry", "ForNode") and pending:
+            if kind == "ForNode":
+                start(True)
+                finish(list(inflight))
+            elif kind not in ("AllocEntry", "DeallocEntry") and (pending or inflight):
                 reads, writes = _accesses(c)
-                touched = set(reads) | set(writes)
-                if any(w in touched for w, _, _, _ in pending):
-                    flush()
+                need(set(reads) | set(writes))
             nodes = c.nodes if isinstance(c, ir.FuseGroup) else [c]
             for i, n in enumerate(nodes):
                 if not _is_update(n, content):
                     continue
                 w = n.kres.id
-                if any(w == pw for pw, _, _, _ in pending):
-                    flush()
+                need({w})
                 n_el = math.prod(n.shape)
                 off = total
                 total += (n_el + 63) // 64 * 64      # 256-byte aligned slices
@@ -131,7 +177,10 @@ def insert_grad_allreduce(proc: ir.Proc, comm=None) -> Optional[int]:
                     c = new
                 pending.append((w, off, n_el, sid))
             new_body.append(c)
-        flush()
+            if 4 * sum(x[2] for x in pending) >= cap:
+                start(True)
+        start(True)
+        finish(list(inflight))
         body.procedure = new_body
         proc.procedure[0:0] = [ir.AllocEntry(gb, total)] + slices
     return gb

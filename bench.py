@@ -287,6 +287,8 @@ def build_parser():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--comm-profile", action="store_true",
+                    help="data parallel: time each gradient all-reduce of one eager iteration")
     ap.add_argument("--no-kernel-timing", action="store_true",
                     help="skip the per-kernel isolated timings (loop workloads)")
     return ap
@@ -490,6 +492,7 @@ def bench_loop(args, wl, rank, world, local, td):
     Lt = launches[top]
     hbm, bf16, peak_kind = peaks()
     kt = max(per_kernel[top], 1e-9) / 1e3
+    timed = not args.no_kernel_timing
     if Lt.spec.kind == "gemm_tcgen05" and not args.no_kernel_timing:
         from ad_b200 import tcgen05
         tf32 = tcgen05.measure_tf32_peak(ctx, dev.err_ptr)
@@ -504,10 +507,13 @@ def bench_loop(args, wl, rank, world, local, td):
                 "frac": achieved / hbm, "traffic": None, "peak_kind": peak_kind}
     roof.update({"kernel": f"{top}:{Lt.spec.kind}", "kernel_ms": float(per_kernel[top]),
                  "alg_bytes": Lt.spec.bytes_moved})
+    if not timed:
+        roof = None                     # --no-kernel-timing: no per-kernel figures
     work_set = dev.arena_bytes + getattr(dev, "scratch_bytes", 0)
     l2_note = (f"step working set {work_set / 1e6:.0f} MB (arena + dot-operand scratch) "
                + ("exceeds the 126 MB L2" if work_set > 126e6 else "fits in the 126 MB L2 (small model)"))
     feed_bytes = sum(4 * int(np.prod(c.shape)) for c in ir.iter_cmds(loop.proc) if type(c).__name__ == "Feeder")
+    comm = comm_profile(dev, loop, td) if (args.comm_profile and dp) else None
     e2e = e2e_loop(dev, proc, loop, args.steps, td)
     if weak:
         value = 1e3 / ms * wl["batch_per_gpu"] * world       # sequences per second, whole job
@@ -532,6 +538,7 @@ def bench_loop(args, wl, rank, world, local, td):
             "per_kernel_GBps": [round(L.spec.bytes_moved / (t / 1e3) / 1e9, 1) if t > 0 else None
                                 for L, t in zip(launches, per_kernel)],
             "clocks": clk.summary(),
+            "comm_profile": comm,
             "e2e": {"value": (value * ms / e2e["ms_per_step"]), "unit": wl["unit"],
                     "ms_per_step": e2e["ms_per_step"], "h2d_bytes_per_step": feed_bytes,
                     "d2h_bytes_per_step": e2e["d2h_bytes"] / args.steps,
@@ -546,6 +553,40 @@ def bench_loop(args, wl, rank, world, local, td):
         print(json.dumps(line), flush=True)
     dev.close()
     barrier(td)
+
+
+def comm_profile(dev, loop, td):
+    """One eager (not graph) iteration of the loop body with CUDA events around
+    every gradient all-reduce; then the same all-reduces alone, back to back."""
+    from ad_b200 import runtime as rt
+    ctx = dev.ctx
+    for _ in range(2):
+        dev.comm_trace = []
+        barrier(td)
+        a, b = ctx.event(True), ctx.event(True)
+        a.record(0)
+        dev._run_proc(loop.proc, dev.run)
+        b.record(0)
+        ctx.sync()
+    it_ms = a.elapsed_ms(b)
+    ops = [{"bytes": n, "async": asy, "ms": round(t0.elapsed_ms(t1), 4),
+            "start_ms": round(a.elapsed_ms(t0), 4)} for n, asy, t0, t1 in dev.comm_trace]
+    dev.comm_trace = None
+    alone = []
+    for op in ops:
+        n = op["bytes"] // 4
+        ctx.sync()
+        barrier(td)
+        e0, e1 = ctx.event(True), ctx.event(True)
+        e0.record(0)
+        for _ in range(5):
+            rt.check(ctx.L.ad_allreduce_f32(ctx.h, dev.arena, dev.arena, n, 0, 0), "ad_allreduce_f32")
+        e1.record(0)
+        e1.sync()
+        alone.append(round(e0.elapsed_ms(e1) / 5, 4))
+    # the allreduces above summed arena contents over ranks; this run is for timing only
+    return {"eager_iteration_ms": round(it_ms, 3), "ops": ops, "alone_ms": alone,
+            "total_bytes": sum(o["bytes"] for o in ops)}
 
 
 def e2e_loop(dev, proc, loop, steps, td):

@@ -354,6 +354,8 @@ class OracleDevice:
             assert isinstance(arr, np.ndarray) and list(arr.shape) == list(c.shape), "Invalid function"
             off = offset_of(c.kres)
             self.buffers[c.kres.id][off:off + arr.size] = arr.reshape(-1)
+        elif kind == "AllReduceWait":
+            pass                      # the oracle's all-reduce is synchronous
         elif kind == "AllReduce":
             # data-parallel gradient sum (ad_b200.dist): the test supplies c.comm
             c.comm(self.buffers[c.buf][c.offset:c.offset + c.count])

@@ -76,10 +76,23 @@ def test_dotsig_4096():
 
 def test_encoder_4_layers_batch32_one_step():
     """Config 4's own proc (4 layers, d512, 8 heads, ff2048, S128, batch 32):
-    every parameter after one SGD step, rel 1e-3."""
+    the SGD update of every parameter after one step, rel 1e-3.
+
+    The update ``p1 - p0 = -lr * grad`` is compared rather than ``p1`` itself:
+    under loss = sum(out) the LayerNorm scales' gradients are sums of 4096
+    normalised activations (magnitude ~100) and lr * grad brings some scales
+    from 1.0 to within 0.05 of zero, so ``p1`` has lost two digits to
+    cancellation that neither computation can avoid."""
+    from ad_b200.fixtures import load_case
     got, want, _ = both("enc_4_32_128_512_8_2048_100", loops=1)
     assert len(got) == len(want) == 4 * (24 + 1 + 4 + 4)
-    assert_parity(got, want, exact_of("enc_4_32_128_512_8_2048_100", loops=1), rtol=1e-3, atol=1e-4)
+    p, m = load_case("enc_4_32_128_512_8_2048_100")
+    init = {c.id: np.asarray(c.content, np.float32) for c in p.procedure
+            if type(c).__name__ == "AllocEntry" and c.content is not None}
+    p0 = [init[i].reshape(g.shape) for i, g in zip(m["param_ids"], got)]
+    exact = exact_of("enc_4_32_128_512_8_2048_100", loops=1)
+    assert_parity([g - a for g, a in zip(got, p0)], [w - a for w, a in zip(want, p0)],
+                  [e - a for e, a in zip(exact, p0)], rtol=1e-3, atol=1e-4)
 
 
 def test_encoder_4_layers_three_steps():
