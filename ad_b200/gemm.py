@@ -6,10 +6,12 @@ epilogue with ``_x = ty, _y = tx, _global_id = ty * wB + tx``
 (opencl/kernels/dp_elw_fuse.py:11-65).  This module picks the B200 schedule:
 
 * ``simt``: fp32 CUDA-core kernels for tiny products where a tensor-core
-  tile would be mostly padding: one warp per output for few outputs with a
+  tile would be mostly padding (or with ``AD_DOT_SMALL=simt``): one warp per output for few outputs with a
   long K (``codegen.gen_dot_warp``), 64x64 register tiles otherwise
   (``codegen.gen_dot_simt``).
-* ``tc``: tcgen05 tensor cores with 3xTF32 (see ``tcgen05.py``).
+* ``tc``: tcgen05 tensor cores with 3xTF32: split operands + persistent GEMM
+  for large products (``tcgen05.py``), one CTA per 128-row tile with the
+  split done in shared memory for small ones (``dot_small.py``).
 """
 from __future__ import annotations
 
@@ -60,7 +62,18 @@ def plan_dot(dev, cmd, name: str, sizes: Dict[int, int]) -> List[codegen.KernelS
         return tcgen05.plan(dev, cmd, name, sizes)
     if K >= 32 and M * N <= 4096:
         return [codegen.gen_dot_warp(cmd, name + "_warp", sizes)]
+    from . import dot_small
+    if use_small_tc(dev, M, N, K):
+        return [dot_small.gen_dot_tc(cmd, name + "_tc", sizes)]
     return [codegen.gen_dot_simt(cmd, name + "_simt", sizes)]
+
+
+def use_small_tc(dev, M: int, N: int, K: int) -> bool:
+    """Products below the grouped-GEMM threshold run on the one-CTA tcgen05
+    kernel (``dot_small``) unless the CUDA-core kernels are asked for."""
+    from . import dot_small
+    mode = os.environ.get("AD_DOT_SMALL", "tc")
+    return mode == "tc" and getattr(dev, "gemm", "auto") != "simt" and dot_small.eligible(M, N, K)
 
 
 def setup_scratch(dev, proc: ir.Proc) -> None:

@@ -29,6 +29,8 @@ of the individual kernels; reductions are exact (see ``codegen.gen_reduce``).
 """
 from __future__ import annotations
 
+import os
+
 import math
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Set, Tuple
@@ -472,6 +474,10 @@ def fuse_rows(proc: ir.Proc) -> ir.Proc:
 STAGE_SMEM_MAX = 96 * 1024   # per block, all ring slots
 # ring depth: 3 slots measured slower than 2 on config 2 (4358 vs ~4550 GB/s)
 MAX_SLOTS = 2
+# threads per row (at most): fewer threads hold more of the row in registers
+# and make each reduction's shuffle/shared-memory exchange cheaper per element
+GS_MAX = int(os.environ.get("AD_RF_GS", "512"))
+GRID_PER_SM = int(os.environ.get("AD_RF_GRID", "2"))     # persistent blocks per SM (staged schedule)
 
 
 def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int = 148) -> KernelSpec:
@@ -484,7 +490,7 @@ def gen_rowfused(rf: RowFused, name: str, sizes: Dict[int, int], sm_count: int =
     V, R = rf.V, rf.R
     units = R // VEC
     gs = 1
-    while gs * 2 <= min(512, units) and units % (gs * 2) == 0:
+    while gs * 2 <= min(GS_MAX, units) and units % (gs * 2) == 0:
         gs *= 2
     nc = units // gs
     if nc > MAX_CHUNKS:
@@ -849,7 +855,7 @@ extern "C" __global__ void __launch_bounds__({block}) {name}({params}) {{
     }}
 }}
 """
-        grid = (min(V, 2 * sm_count), 1, 1)
+        grid = (min(V, GRID_PER_SM * sm_count), 1, 1)
         smem = stage_bytes
     # algorithmic bytes: external reads + external writes (extents)
     nbytes = 0

@@ -62,8 +62,25 @@ def tile_n(N: int) -> int:
 
 # ---------------------------------------------------------------- split kernel
 
+_SPLIT_CACHE: Dict[tuple, KernelSpec] = {}
+
+
 def gen_split(karg: ir.KernelArg, name: str, rows: int, kdim: int, rows_p: int, k_p: int,
               row_var: str, k_var: str) -> KernelSpec:
+    """``_gen_split`` memoised on the operand's value (a large proc asks for the
+    same operand's split source many times while grouping and planning)."""
+    import dataclasses
+    key = (repr(karg), name, rows, kdim, rows_p, k_p, row_var, k_var)
+    sp = _SPLIT_CACHE.get(key)
+    if sp is None:
+        if len(_SPLIT_CACHE) > 200000:
+            _SPLIT_CACHE.clear()
+        sp = _SPLIT_CACHE[key] = _gen_split(karg, name, rows, kdim, rows_p, k_p, row_var, k_var)
+    return dataclasses.replace(sp, extra=dict(sp.extra))
+
+
+def _gen_split(karg: ir.KernelArg, name: str, rows: int, kdim: int, rows_p: int, k_p: int,
+               row_var: str, k_var: str) -> KernelSpec:
     """Gather operand(row, k) via its access expression into K-major hi/lo
     arrays (``rows_p`` x ``k_p``, zero-padded).  ``row_var``/``k_var`` say which
     of the reference's X/Y carries row and k.

@@ -45,3 +45,18 @@ def test_host_copy_threads():
         dst = np.zeros(n + 16, np.uint8)
         rt.host_copy(dst.ctypes.data, src.ctypes.data, n)
         assert np.array_equal(dst[:n], src) and not dst[n:].any()
+
+
+def test_small_dot_kernel_compiles_for_sm100a():
+    """The one-CTA tcgen05 dot kernel (dot_small) builds for the encoder's
+    attention shapes, with ptxas's limits met (NVRTC straight to a cubin)."""
+    from ad_b200 import dot_small
+    from tests.procgen import dot_proc
+    import numpy as np
+    for M, N, K, tb in ((128, 128, 64, True), (128, 64, 128, False), (130, 300, 17, True)):
+        proc = dot_proc(np.zeros((M, K), np.float32), np.zeros((N, K) if tb else (K, N), np.float32),
+                        transpose_b=tb)
+        cmd = next(c for c in proc.procedure if type(c).__name__ in ("DotProdNode", "DPElwFuse"))
+        sp = dot_small.gen_dot_tc(cmd, "k_dot_tc", {})
+        assert sp.kind == "dot_tc" and sp.smem <= 225 * 1024
+        assert len(rt.compile_cubin(sp.src, "k_dot_tc.cu")) > 1000

@@ -47,3 +47,34 @@ def test_dot_epilogue_bias_scale():
     want = (A.astype(np.float64) @ B + b) * -0.5
     mag = (np.abs(A).astype(np.float64) @ np.abs(B) + np.abs(b)) * 0.5
     assert np.all(np.abs(got - want) <= 1e-4 * mag + 1e-5)
+
+
+@pytest.mark.parametrize("M,N,K,tb", [(128, 128, 64, True), (128, 64, 128, False), (64, 128, 128, True),
+                                      (100, 70, 40, False), (128, 300, 96, True), (256, 32, 16, False),
+                                      (130, 33, 17, True), (384, 128, 200, False)])
+def test_small_dot_tcgen05(M, N, K, tb):
+    """Products below the grouped-GEMM threshold: one-CTA tcgen05 kernel with
+    the hi/lo split done in shared memory (``dot_small``); ragged M, N, K, a
+    transposed operand, two column tiles, several K chunks."""
+    rng = np.random.default_rng(M * 5 + N * 3 + K)
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (N, K) if tb else (K, N)).astype(np.float32)
+    Bm = B.T if tb else B
+    got, kinds = run(dot_proc(A, B, transpose_b=tb), "auto")
+    assert kinds == ["dot_tc"], kinds
+    want = A.astype(np.float64) @ Bm.astype(np.float64)
+    mag = np.abs(A).astype(np.float64) @ np.abs(Bm).astype(np.float64)
+    assert np.all(np.abs(got - want) <= 1e-4 * mag + 1e-5)
+
+
+def test_small_dot_epilogue_bias_scale():
+    rng = np.random.default_rng(2)
+    M, N, K = 128, 96, 64
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    got, kinds = run(dot_proc(A, B, bias=b, epi_scale=-0.5), "auto")
+    assert kinds == ["dot_tc"], kinds
+    want = (A.astype(np.float64) @ B + b) * -0.5
+    mag = (np.abs(A).astype(np.float64) @ np.abs(B) + np.abs(b)) * 0.5
+    assert np.all(np.abs(got - want) <= 1e-4 * mag + 1e-5)
