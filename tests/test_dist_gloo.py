@@ -93,3 +93,34 @@ def test_rewrite_without_peers_is_identity():
     o2.execute(q)
     for g, w in zip(o2.last_received, o.last_received):
         np.testing.assert_array_equal(g, w)
+
+
+def test_async_buckets_overlap_backward():
+    """Bucketed all-reduces start as soon as their gradients exist and are
+    joined as late as the next reader allows: on the 4-layer encoder's rank
+    proc some join sits several commands after its start, every join precedes
+    the updates of its members, and the buckets tile the gradient buffer."""
+    from ad_b200.device import CudaB200Device
+    p, _ = load_case("enc_4_32_128_512_8_2048_100_p2")
+    q = CudaB200Device.passes_only(p, world=2)
+    loop = next(c for c in q.procedure if type(c).__name__ == "ForNode")
+    body = loop.proc.procedure
+    starts = {id(c): i for i, c in enumerate(body) if type(c).__name__ == "AllReduce"}
+    assert starts and all(c.async_start for c in body if type(c).__name__ == "AllReduce")
+    gaps, n_updates = [], [0]
+    for i, c in enumerate(body):
+        if type(c).__name__ != "AllReduceWait":
+            continue
+        for s in c.starts:
+            assert starts[id(s)] < i
+            gaps.append(i - starts[id(s)])
+            members = set(s.members)
+            for j, u in enumerate(body):
+                for v in (u.cmds if type(u).__name__ == "Batched" else [u]):
+                    if type(v).__name__ == "BinaryNode" and v.in_place and \
+                            any(getattr(k, "id", None) in members for k in v.kargs):
+                        assert j > i
+                        n_updates[0] += 1
+    assert max(gaps) >= 5 and n_updates[0] == 4 * 33
+    ars = sorted((c.offset, c.offset + c.count) for c in body if type(c).__name__ == "AllReduce")
+    assert ars[0][0] == 0 and all(a[1] == b[0] for a, b in zip(ars, ars[1:]))
