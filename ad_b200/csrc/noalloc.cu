@@ -25,9 +25,12 @@
 //     cudaGetSymbolAddress (the host-side name of a __device__ array is only a
 //     stand-in, not a device address) and raises the kernel's shared-memory
 //     limit; make that first call outside any stream capture.
-//   * The call waits for its own work to finish so that it can report a
-//     device-side timeout; it never calls cudaMalloc, cudaFree or any
-//     allocating library routine.
+//   * Every call ends by synchronising its stream (it copies the kernel's
+//     status word to the host) so that it can report a device-side timeout;
+//     it never calls cudaMalloc, cudaFree or any allocating library routine.
+//   * The array's address and the shared-memory limit are cached per device
+//     for the life of the process; after cudaDeviceReset on a device they are
+//     stale, so do not call this entry point on a device that was reset.
 #include <cuda.h>
 #include <cuda_runtime.h>
 

@@ -141,7 +141,9 @@ int ad_nccl_abort(ad_ctx* ctx);
  * All calls share that array: calls that overlap on one GPU race.  The first
  * call on each device resolves the array's address (cudaGetSymbolAddress), so
  * make it before any stream capture.  `stream` is a cudaStream_t (NULL = the
- * legacy default stream); the call returns after its work has finished. */
+ * legacy default stream); the call returns after its work has finished.
+ * The resolved address is kept for the life of the process: do not call this
+ * on a device after cudaDeviceReset. */
 int ad_dot_tf32x3_noalloc(const float* A, const float* B, float* C, int M, int N, int K,
                           int b_is_nk, void* stream);
 
