@@ -79,18 +79,8 @@ def gen_dot_tc(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
     epi = "\n                    ".join(epi.split("\n"))
     params = ", ".join([f"float* __restrict__ p{i}" for i in range(len(bufs))] + ["int* __restrict__ err"])
 
-    def contiguous(k, var):
-        return isinstance(k, ir.KMatrix) and not k.is_temp and exprs.lanes(k.access, var, 4).s == 1
-
-    # consecutive threads walk each operand's contiguous dimension
-    if contiguous(A, "X") and not contiguous(A, "Y"):
-        a_idx = "const int r = e % 128, k = e / 128;"
-    else:
-        a_idx = f"const int k = e % {KC}, r = e / {KC};"
-    if contiguous(B, "X") and not contiguous(B, "Y"):
-        b_idx = f"const int k = e % {KC}, r = e / {KC};"
-    else:
-        b_idx = f"const int r = e % {BN}, k = e / {BN};"
+    a_fill = _fill(em, A, "A", "Ah", "Al", 128, KC, M, K, "m0", "X", "Y", it)
+    b_fill = _fill(em, B, "B", "Bh", "Bl", BN, KC, N, K, "n0", "Y", "X", it)
     A_BYTES, B_BYTES = 128 * KC * 4, BN * KC * 4
     # + alignment slack; the epilogue's 8 x 4 KB transpose buffers reuse the operands
     smem = max(A_BYTES * 2 + B_BYTES * 2, 32 * 1024) + 1024
@@ -130,6 +120,13 @@ __device__ __forceinline__ void ds_split(float x, float& h, float& l) {{
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lb) : "f"(x - __uint_as_float(hb)));
     h = __uint_as_float(hb);
     l = __uint_as_float(lb);
+}}
+__device__ __forceinline__ void ds_put4(float* H, float* L, unsigned o, float4 v) {{
+    // 4 consecutive k of one row: one 16-byte chunk of the swizzled layout
+    float4 h, l;
+    ds_split(v.x, h.x, l.x); ds_split(v.y, h.y, l.y); ds_split(v.z, h.z, l.z); ds_split(v.w, h.w, l.w);
+    *reinterpret_cast<float4*>(H + o) = h;
+    *reinterpret_cast<float4*>(L + o) = l;
 }}
 __device__ __forceinline__ unsigned long long ds_desc(const void* p) {{
     // start >> 4, LBO 16 B (unused with swizzling), SBO = 8 rows x 64 B, version 1, SWIZZLE_64B
@@ -174,26 +171,8 @@ extern "C" __global__ void __launch_bounds__(256, 1) {name}({params}) {{
             }}
         }}
         const {it} k0 = ({it})ch * {KC};
-        for (int e = threadIdx.x; e < {128 * KC}; e += 256) {{
-            {a_idx}
-            const {it} gm = m0 + r, gk = k0 + k;
-            const float x = (gm < ({it}){M} && gk < ({it}){K}) ? ({la}) : 0.0f;
-            float h, l;
-            ds_split(x, h, l);
-            const unsigned o = ds_off(r, k, 128) >> 2;
-            Ah[o] = h;
-            Al[o] = l;
-        }}
-        for (int e = threadIdx.x; e < {BN * KC}; e += 256) {{
-            {b_idx}
-            const {it} gn = n0 + r, gk = k0 + k;
-            const float x = (gn < ({it}){N} && gk < ({it}){K}) ? ({lb}) : 0.0f;
-            float h, l;
-            ds_split(x, h, l);
-            const unsigned o = ds_off(r, k, {BN}) >> 2;
-            Bh[o] = h;
-            Bl[o] = l;
-        }}
+{a_fill}
+{b_fill}
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
         if (threadIdx.x == 0) {{
@@ -274,3 +253,63 @@ extern "C" __global__ void __launch_bounds__(256, 1) {name}({params}) {{
                       written_reads_bytes(c, rngw, sizes), 2 * M * N * K)
     spec.extra["err_param"] = True
     return spec
+
+
+def _fill(em, karg, tag: str, H: str, L: str, rows: int, KC: int, extent_r: int, extent_k: int,
+          base: str, row_var: str, k_var: str, it: str) -> str:
+    """Code gathering one K chunk of an operand (rows x KC of element (r, k) =
+    karg at {row_var: base + r, k_var: k0 + k}, zero outside the extents) into
+    the hi/lo shared-memory tiles.  Work items are 4 x 4 blocks: four k of one
+    row (k-contiguous operands, one 16-byte load) or four rows of one k
+    (row-contiguous operands: four 16-byte loads, transposed in registers);
+    each item writes four 16-byte chunks of hi and of lo."""
+    plain = isinstance(karg, ir.KMatrix) and not karg.is_temp
+    k_contig = plain and exprs.lanes(karg.access, k_var, 4).s == 1
+    r_contig = plain and exprs.lanes(karg.access, row_var, 4).s == 1
+    orient = "k" if (k_contig or not r_contig) else "r"
+    lane_var = k_var if orient == "k" else row_var
+    other = row_var if orient == "k" else k_var
+    vec = plain and exprs.lanes(karg.access, lane_var, 4, {other: 1}).unit(4)
+
+    def load4(dst, ga, gb):
+        """4 consecutive values along the lane axis from (ga .. ga+3, gb)."""
+        lane_ext, other_ext = (extent_k, extent_r) if orient == "k" else (extent_r, extent_k)
+
+        def env(ga_, gb_):
+            d = {k_var: ga_, row_var: gb_} if orient == "k" else {row_var: ga_, k_var: gb_}
+            d["G"] = f"(({it})0)"
+            return d
+        out = [f"float4 {dst} = make_float4(0.0f, 0.0f, 0.0f, 0.0f);",
+               f"if ({gb} < ({it}){other_ext}) {{"]
+        if vec:
+            out.append(f"    if ({ga} + 3 < ({it}){lane_ext}) {dst} = "
+                       f"*reinterpret_cast<const float4*>(&{em.at(karg, env(ga, gb))});")
+            out.append("    else {")
+        else:
+            out.append("    {")
+        for j, comp in enumerate("xyzw"):
+            out.append(f"        if ({ga} + {j} < ({it}){lane_ext}) {dst}.{comp} = "
+                       f"{em.scalar_karg(karg, env(f'({ga} + {j})', gb), {})};")
+        out += ["    }", "}"]
+        return "\n            ".join(out)
+
+    if orient == "k":
+        n_items = rows * (KC // 4)
+        body = f"""            const int r = e / {KC // 4}, k = (e % {KC // 4}) * 4;
+            const {it} gr = {base} + r, gk = k0 + k;
+            {load4("v", "gk", "gr")}
+            ds_put4({H}, {L}, ds_off(r, k, {rows}) >> 2, v);"""
+    else:
+        n_items = (rows // 4) * (KC // 4)
+        loads = "\n            ".join(load4(f"c{j}", "gr", f"(gk + {j})") for j in range(4))
+        body = f"""            const int r = (e % {rows // 4}) * 4, k = (e / {rows // 4}) * 4;
+            const {it} gr = {base} + r, gk = k0 + k;
+            {loads}
+            ds_put4({H}, {L}, ds_off(r + 0, k, {rows}) >> 2, make_float4(c0.x, c1.x, c2.x, c3.x));
+            ds_put4({H}, {L}, ds_off(r + 1, k, {rows}) >> 2, make_float4(c0.y, c1.y, c2.y, c3.y));
+            ds_put4({H}, {L}, ds_off(r + 2, k, {rows}) >> 2, make_float4(c0.z, c1.z, c2.z, c3.z));
+            ds_put4({H}, {L}, ds_off(r + 3, k, {rows}) >> 2, make_float4(c0.w, c1.w, c2.w, c3.w));"""
+    return f"""        // operand {tag}: {'k' if orient == 'k' else 'row'}-contiguous gather{' (16-byte loads)' if vec else ''}
+        for (int e = threadIdx.x; e < {n_items}; e += 256) {{
+{body}
+        }}"""

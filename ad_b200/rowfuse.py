@@ -474,9 +474,10 @@ def fuse_rows(proc: ir.Proc) -> ir.Proc:
 STAGE_SMEM_MAX = 96 * 1024   # per block, all ring slots
 # ring depth: 3 slots measured slower than 2 on config 2 (4358 vs ~4550 GB/s)
 MAX_SLOTS = 2
-# threads per row (at most): fewer threads hold more of the row in registers
+# threads per row (at most; 256 measured 5.9 vs 4.7 TB/s for 512 on config 2):
+# fewer threads hold more of the row in registers
 # and make each reduction's shuffle/shared-memory exchange cheaper per element
-GS_MAX = int(os.environ.get("AD_RF_GS", "512"))
+GS_MAX = int(os.environ.get("AD_RF_GS", "256"))
 GRID_PER_SM = int(os.environ.get("AD_RF_GRID", "2"))     # persistent blocks per SM (staged schedule)
 
 

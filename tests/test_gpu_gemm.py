@@ -51,7 +51,7 @@ def test_dot_epilogue_bias_scale():
 
 @pytest.mark.parametrize("M,N,K,tb", [(128, 128, 64, True), (128, 64, 128, False), (64, 128, 128, True),
                                       (100, 70, 40, False), (128, 300, 96, True), (256, 32, 16, False),
-                                      (130, 33, 17, True), (384, 128, 200, False)])
+                                      (130, 33, 17, True), (384, 96, 100, False)])
 def test_small_dot_tcgen05(M, N, K, tb):
     """Products below the grouped-GEMM threshold: one-CTA tcgen05 kernel with
     the hi/lo split done in shared memory (``dot_small``); ragged M, N, K, a
