@@ -86,10 +86,13 @@ def test_encoder_4_layers_batch32_one_step():
     from ad_b200.fixtures import load_case
     got, want, _ = both("enc_4_32_128_512_8_2048_100", loops=1)
     assert len(got) == len(want) == 4 * (24 + 1 + 4 + 4)
+    from ad_b200 import ir
+    from ad_b200.device import offset_of
     p, m = load_case("enc_4_32_128_512_8_2048_100")
-    init = {c.id: np.asarray(c.content, np.float32) for c in p.procedure
+    init = {c.id: np.asarray(c.content, np.float32).reshape(-1) for c in ir.iter_cmds(p)
             if type(c).__name__ == "AllocEntry" and c.content is not None}
-    p0 = [init[i].reshape(g.shape) for i, g in zip(m["param_ids"], got)]
+    rec = next(c for c in ir.iter_cmds(p) if type(c).__name__ == "Receiver")
+    p0 = [init[k.id][offset_of(k):offset_of(k) + g.size].reshape(g.shape) for k, g in zip(rec.kargs, got)]
     exact = exact_of("enc_4_32_128_512_8_2048_100", loops=1)
     assert_parity([g - a for g, a in zip(got, p0)], [w - a for w, a in zip(want, p0)],
                   [e - a for e, a in zip(exact, p0)], rtol=1e-3, atol=1e-4)
