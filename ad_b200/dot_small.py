@@ -79,8 +79,8 @@ def gen_dot_tc(c, name: str, sizes: Dict[int, int]) -> KernelSpec:
     epi = "\n                    ".join(epi.split("\n"))
     params = ", ".join([f"float* __restrict__ p{i}" for i in range(len(bufs))] + ["int* __restrict__ err"])
 
-    a_fill = _fill(em, A, "A", "Ah", "Al", 128, KC, M, K, "m0", "X", "Y", it)
-    b_fill = _fill(em, B, "B", "Bh", "Bl", BN, KC, N, K, "n0", "Y", "X", it)
+    a_load, a_store = _fill(em, A, "A", "Ah", "Al", 128, KC, M, K, "m0", "X", "Y", it)
+    b_load, b_store = _fill(em, B, "B", "Bh", "Bl", BN, KC, N, K, "n0", "Y", "X", it)
     A_BYTES, B_BYTES = 128 * KC * 4, BN * KC * 4
     # + alignment slack; the epilogue's 8 x 4 KB transpose buffers reuse the operands
     smem = max(A_BYTES * 2 + B_BYTES * 2, 32 * 1024) + 1024
@@ -171,8 +171,10 @@ extern "C" __global__ void __launch_bounds__(256, 1) {name}({params}) {{
             }}
         }}
         const {it} k0 = ({it})ch * {KC};
-{a_fill}
-{b_fill}
+{a_load}
+{b_load}
+{a_store}
+{b_store}
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
         if (threadIdx.x == 0) {{
@@ -293,23 +295,47 @@ def _fill(em, karg, tag: str, H: str, L: str, rows: int, KC: int, extent_r: int,
         out += ["    }", "}"]
         return "\n            ".join(out)
 
+    # all of a thread's loads are issued before any shared-memory store (the
+    # stores go through generic pointers the compiler cannot separate from the
+    # loads), so the chunk's global reads overlap instead of running one by one
     if orient == "k":
         n_items = rows * (KC // 4)
-        body = f"""            const int r = e / {KC // 4}, k = (e % {KC // 4}) * 4;
-            const {it} gr = {base} + r, gk = k0 + k;
-            {load4("v", "gk", "gr")}
-            ds_put4({H}, {L}, ds_off(r, k, {rows}) >> 2, v);"""
+        nit = -(-n_items // 256)
+        idx = f"const int r = e / {KC // 4}, k = (e % {KC // 4}) * 4;"
+        loads = f"""const {it} gr = {base} + r, gk = k0 + k;
+                {load4("v", "gk", "gr")}
+                {tag}v[i_] = v;"""
+        stores = f"ds_put4({H}, {L}, ds_off(r, k, {rows}) >> 2, {tag}v[i_]);"
+        decl = f"float4 {tag}v[{nit}];"
     else:
         n_items = (rows // 4) * (KC // 4)
-        loads = "\n            ".join(load4(f"c{j}", "gr", f"(gk + {j})") for j in range(4))
-        body = f"""            const int r = (e % {rows // 4}) * 4, k = (e / {rows // 4}) * 4;
-            const {it} gr = {base} + r, gk = k0 + k;
-            {loads}
-            ds_put4({H}, {L}, ds_off(r + 0, k, {rows}) >> 2, make_float4(c0.x, c1.x, c2.x, c3.x));
-            ds_put4({H}, {L}, ds_off(r + 1, k, {rows}) >> 2, make_float4(c0.y, c1.y, c2.y, c3.y));
-            ds_put4({H}, {L}, ds_off(r + 2, k, {rows}) >> 2, make_float4(c0.z, c1.z, c2.z, c3.z));
-            ds_put4({H}, {L}, ds_off(r + 3, k, {rows}) >> 2, make_float4(c0.w, c1.w, c2.w, c3.w));"""
-    return f"""        // operand {tag}: {'k' if orient == 'k' else 'row'}-contiguous gather{' (16-byte loads)' if vec else ''}
-        for (int e = threadIdx.x; e < {n_items}; e += 256) {{
-{body}
+        nit = -(-n_items // 256)
+        idx = f"const int r = (e % {rows // 4}) * 4, k = (e / {rows // 4}) * 4;"
+        ld = "\n                ".join(load4(f"c{j}", "gr", f"(gk + {j})") + f"\n                {tag}c{j}[i_] = c{j};"
+                                       for j in range(4))
+        loads = f"""const {it} gr = {base} + r, gk = k0 + k;
+                {ld}"""
+        stores = "\n                ".join(
+            f"ds_put4({H}, {L}, ds_off(r + {q}, k, {rows}) >> 2, make_float4({tag}c0[i_].{cmp}, {tag}c1[i_].{cmp}, "
+            f"{tag}c2[i_].{cmp}, {tag}c3[i_].{cmp}));" for q, cmp in enumerate("xyzw"))
+        decl = " ".join(f"float4 {tag}c{j}[{nit}];" for j in range(4))
+    guard = "" if n_items % 256 == 0 else f"if (e < {n_items}) "
+    load_code = f"""        // operand {tag}: {'k' if orient == 'k' else 'row'}-contiguous gather{' (16-byte loads)' if vec else ''}
+        {decl}
+        #pragma unroll
+        for (int i_ = 0; i_ < {nit}; ++i_) {{
+            const int e = threadIdx.x + i_ * 256;
+            {guard}{{
+                {idx}
+                {loads}
+            }}
         }}"""
+    store_code = f"""        #pragma unroll
+        for (int i_ = 0; i_ < {nit}; ++i_) {{
+            const int e = threadIdx.x + i_ * 256;
+            {guard}{{
+                {idx}
+                {stores}
+            }}
+        }}"""
+    return load_code, store_code
