@@ -29,6 +29,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -248,7 +249,12 @@ class CopyPool {
  private:
   CopyPool() {
     unsigned hw = std::thread::hardware_concurrency();
-    unsigned nw = hw > 2 ? (hw / 2 < 8 ? hw / 2 : 8) - 1 : 0;
+    unsigned want = hw > 2 ? (hw / 2 < 8 ? hw / 2 : 8) : 1;
+    if (const char* e = getenv("AD_COPY_THREADS")) {  // threads incl. the caller
+      int v = atoi(e);
+      if (v >= 1 && v <= 64) want = (unsigned)v;
+    }
+    unsigned nw = want - 1;
     for (unsigned i = 0; i < nw; ++i) workers_.emplace_back([this] { run(); });
   }
   ~CopyPool() {

@@ -86,6 +86,11 @@ class CudaB200Device:
         the 128-byte NCCL id from ``ad_b200.dist.nccl_unique_id()`` on rank 0,
         shared with every rank by the caller.  The proc is then this rank's shard
         and gradients are summed over ranks (``ad_b200.dist``)."""
+        # host copy threads (pageable Feeder/Receiver staging): share the cores
+        # among the processes of this node
+        lw = int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
+        if lw > 1 and "AD_COPY_THREADS" not in os.environ:
+            os.environ["AD_COPY_THREADS"] = str(max(1, (os.cpu_count() or 2) // (2 * lw)))
         self.ctx = rt.Context(device)
         self.world = 1
         if dp is not None and dp[1] > 1:
@@ -486,7 +491,8 @@ class CudaB200Device:
         all-reduce rewrite (data parallel), splitting of horizontally fused
         elementwise groups, row fusion, and batching."""
         proc = ir.copy_structure(ir.conv_proc(proc))
-        if self.world > 1:
+        if self.world > 1 or os.environ.get("AD_DP_FORCE_REWRITE") == "1":
+            # (forced on one GPU with AD_DP_SKIP_COMM=1: profiles the rewrite's own cost)
             from . import dist
             dist.insert_grad_allreduce(proc)
         if self.hsplit:
