@@ -296,6 +296,9 @@ def build_parser():
 
 def main():
     args = build_parser().parse_args()
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # NCCL's init lines name the communicator's rank count and its algorithms (NVLS)
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
     args.warmup = max(args.warmup, 3)
     wl = WORKLOADS[args.workload]
     rank, world, local = dist_env()
@@ -447,9 +450,6 @@ def bench_loop(args, wl, rank, world, local, td):
         if not weak:
             case = f"{case}_p{world}"
         from ad_b200 import dist
-        # NCCL's init lines name the communicator's rank count (and NVLS use)
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         box = [dist.nccl_unique_id() if rank == 0 else None]
         td.broadcast_object_list(box, src=0)
         dp = (rank, world, box[0])
