@@ -391,6 +391,7 @@ class CudaB200Device:
         return np.ctypeslib.as_array((ctypes.c_float * (nbytes // 4)).from_address(p.value))
 
     LOOP_UNROLL = 16
+    FIRST_CHUNK = 2
 
     def _loop_graphs(self, loop: ir.ForNode, feeders, u: int):
         """Two graphs (ping-pong) of ``u`` iterations each, with their own pinned
@@ -412,7 +413,11 @@ class CudaB200Device:
         feeders = [c for c in ir.iter_cmds(loop.proc) if type(c).__name__ == "Feeder"]
         n = len(loop.r)
         u = max(1, min(n, self.LOOP_UNROLL))
-        chunks = [u] * (n // u) + ([n % u] if n % u else [])
+        # a short first chunk: its Feeder data is staged on the host before the
+        # GPU has anything to run, later chunks are staged while the previous one runs
+        first = min(n, self.FIRST_CHUNK) if feeders and n > u else 0
+        rest = n - first
+        chunks = ([first] if first else []) + [u] * (rest // u) + ([rest % u] if rest % u else [])
         n_kern = sum(len(self.launches.get(id(c), [])) for c in ir.iter_cmds(loop.proc))
         for ci, cu in enumerate(chunks):
             pairs = self._loop_graphs(loop, feeders, cu)

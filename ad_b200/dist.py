@@ -116,17 +116,31 @@ def insert_grad_allreduce(proc: ir.Proc, comm=None, bucket_bytes: Optional[int] 
         new_body: List = []
         slices: List[ir.AllocEntry] = []
 
-        def start(async_start: bool):
+        def start(async_start: bool, which=None):
+            """Start the all-reduce of ``which`` (default: every pending slice),
+            one collective per run of adjacent slices in the bucket."""
             nonlocal pending
-            if not pending:
+            which = pending if which is None else which
+            if not which:
                 return
-            start_off = pending[0][1]
-            end_off = pending[-1][1] + (pending[-1][2] + 63) // 64 * 64
-            ar = AllReduce(gb, end_off - start_off, start_off,
-                           tuple(sid for _, _, _, sid in pending), comm=comm, async_start=async_start)
-            new_body.append(ar)
-            inflight.append((ar, pending))
-            pending = []
+            runs, cur = [], [which[0]]
+            for x in which[1:]:
+                prev = cur[-1]
+                if x[1] == prev[1] + (prev[2] + 63) // 64 * 64:
+                    cur.append(x)
+                else:
+                    runs.append(cur)
+                    cur = [x]
+            runs.append(cur)
+            for run in runs:
+                start_off = run[0][1]
+                end_off = run[-1][1] + (run[-1][2] + 63) // 64 * 64
+                ar = AllReduce(gb, end_off - start_off, start_off,
+                               tuple(sid for _, _, _, sid in run), comm=comm, async_start=async_start)
+                new_body.append(ar)
+                inflight.append((ar, run))
+            ids = {id(x) for x in which}
+            pending = [x for x in pending if id(x) not in ids]
 
         def finish(which):
             """Wait for the started buckets ``which`` and apply their updates."""
@@ -145,7 +159,9 @@ def insert_grad_allreduce(proc: ir.Proc, comm=None, bucket_bytes: Optional[int] 
 
         def need(params):
             """Every update of ``params`` must be applied before the next command."""
-            if any(w in params for w, _, _, _ in pending):
+            if any(x[0] in params for x in pending):
+                # everything pending goes with it: per-parameter collectives for
+                # the per-head weights would put dozens of latencies on the path
                 start(True)
             finish([x for x in inflight if any(w in params for w, _, _, _ in x[1])])
 
