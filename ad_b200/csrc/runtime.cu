@@ -651,37 +651,6 @@ int ad_launch(ad_ctx* c, ad_kernel* k, unsigned gx, unsigned gy, unsigned gz, un
   return 0;
 }
 
-int ad_launch_pdl(ad_ctx* c, ad_kernel* k, unsigned gx, unsigned gy, unsigned gz, unsigned bx,
-                  unsigned by, unsigned bz, unsigned smem, void** args, int stream) {
-  cudaStream_t s;
-  if (stream_of(c, stream, &s)) return 1;
-  if (!k) return fail("null kernel");
-  CUlaunchAttribute attr[1];
-  memset(attr, 0, sizeof(attr));
-  attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
-  attr[0].value.programmaticStreamSerializationAllowed = 1;
-  CUlaunchConfig cfg;
-  memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDimX = gx;
-  cfg.gridDimY = gy;
-  cfg.gridDimZ = gz;
-  cfg.blockDimX = bx;
-  cfg.blockDimY = by;
-  cfg.blockDimZ = bz;
-  cfg.sharedMemBytes = smem;
-  cfg.hStream = (CUstream)s;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  CUresult r = g_drv.launchKernelEx(&cfg, k->fn, args, nullptr);
-  if (r != CUDA_SUCCESS) {
-    char what[256];
-    snprintf(what, sizeof(what), "cuLaunchKernelEx(%s grid=%u,%u,%u block=%u,%u,%u smem=%u, PDL)",
-             k->name.c_str(), gx, gy, gz, bx, by, bz, smem);
-    return cu_fail(r, what);
-  }
-  return 0;
-}
-
 int ad_check(ad_ctx* c) {
   if (set_dev(c)) return 1;
   CK(cudaGetLastError());

@@ -29,7 +29,6 @@ from __future__ import annotations
 import ctypes
 import math
 import os
-import re
 import time
 from concurrent.futures import ThreadPoolExecutor
 from typing import Callable, Dict, List, Optional
@@ -43,21 +42,6 @@ ELEMENTWISE = ("ElwFuse", "BinaryNode", "UnaryNode", "ContigiousNode")
 REDUCE = ("ReduceNode", "ReduceElwFuse")
 DOT = ("DotProdNode", "DPElwFuse")
 COMM_STREAM = 3          # the context's communication stream (include/ad_b200.h)
-
-
-_KERNEL_OPEN = re.compile(r'(extern "C" __global__ void [^{]*\{)')
-
-
-def with_pdl(src: str) -> str:
-    """Kernel source for programmatic dependent launch: wait for the previous
-    kernel on the stream to complete (and its writes to be visible) before
-    anything else, then let the next kernel's blocks be scheduled as SMs free up."""
-    out, n = _KERNEL_OPEN.subn(
-        r'\1\n    asm volatile("griddepcontrol.wait;" ::: "memory");'
-        r'\n    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");', src, count=1)
-    if n != 1:
-        raise ValueError("kernel entry not found")
-    return out
 
 
 class Launch:
@@ -101,9 +85,6 @@ class CudaB200Device:
         self.rowfuse = rowfuse and os.environ.get("AD_ROWFUSE", "1") != "0"
         self.batch = batch and os.environ.get("AD_BATCH", "1") != "0"
         self.hsplit = hsplit and os.environ.get("AD_HSPLIT", "1") != "0"
-        # programmatic dependent launch: measured no gain on the encoder step
-        # (5.25 vs 5.15 ms), so opt-in
-        self.pdl = os.environ.get("AD_PDL", "0") == "1"
         self._spec_cache: Dict[int, codegen.KernelSpec] = {}
         self.use_graphs = use_graphs and os.environ.get("AD_GRAPH", "1") != "0"
         self.gemm = os.environ.get("AD_GEMM", gemm)
@@ -253,7 +234,7 @@ class CudaB200Device:
         t0 = time.time()
         srcs = list(todo.values())
         with ThreadPoolExecutor(max_workers=min(16, max(1, len(srcs)))) as ex:
-            cubins = list(ex.map(lambda s: rt.compile_cubin(with_pdl(s.src) if self.pdl else s.src,
+            cubins = list(ex.map(lambda s: rt.compile_cubin(s.src,
                                                             s.name + ".cu"), srcs))
         for s, cub in zip(srcs, cubins):
             k = self.ctx.load(cub, s.name)
@@ -283,7 +264,7 @@ class CudaB200Device:
     # ------------------------------------------------------------ run pass
     def _launch(self, L: Launch, stream: int = 0) -> None:
         s = L.spec
-        self.ctx.launch(L.kernel, s.grid, s.block, s.smem, L.argv, stream, self.pdl)
+        self.ctx.launch(L.kernel, s.grid, s.block, s.smem, L.argv, stream)
         self.n_launches += 1
 
     def run(self, cmd) -> None:

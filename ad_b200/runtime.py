@@ -59,8 +59,6 @@ SIGNATURES = {
     "ad_kernel_attr": (c_int, [c_void_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     "ad_launch": (c_int, [c_void_p, c_void_p, c_uint, c_uint, c_uint, c_uint, c_uint, c_uint, c_uint,
                           ctypes.POINTER(c_void_p), c_int]),
-    "ad_launch_pdl": (c_int, [c_void_p, c_void_p, c_uint, c_uint, c_uint, c_uint, c_uint, c_uint, c_uint,
-                              ctypes.POINTER(c_void_p), c_int]),
     "ad_check": (c_int, [c_void_p]),
     "ad_tmap_2d": (c_int, [c_u64, c_u64, c_u64, c_u64, c_u32, c_u32, c_int, c_int, c_void_p]),
     "ad_graph_begin": (c_int, [c_void_p, c_int]),
@@ -218,13 +216,10 @@ class Context:
     def load(self, cubin: bytes, fn: str) -> "Kernel":
         return Kernel(self, cubin, fn)
 
-    def launch(self, k: "Kernel", grid, block, smem: int, args, stream: int = 0, pdl: bool = False) -> None:
+    def launch(self, k: "Kernel", grid, block, smem: int, args, stream: int = 0) -> None:
         gx, gy, gz = (tuple(grid) + (1, 1))[:3]
         bx, by, bz = (tuple(block) + (1, 1))[:3]
-        if pdl:
-            check(self.L.ad_launch_pdl(self.h, k.h, gx, gy, gz, bx, by, bz, smem, args, stream), "ad_launch_pdl")
-        else:
-            check(self.L.ad_launch(self.h, k.h, gx, gy, gz, bx, by, bz, smem, args, stream), "ad_launch")
+        check(self.L.ad_launch(self.h, k.h, gx, gy, gz, bx, by, bz, smem, args, stream), "ad_launch")
 
     def close(self) -> None:
         if self.h:

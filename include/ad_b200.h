@@ -99,12 +99,6 @@ int ad_kernel_attr(ad_kernel* k, int* regs, int* static_smem, int* max_threads);
  * `args` is the usual array of pointers to each kernel parameter. */
 int ad_launch(ad_ctx* ctx, ad_kernel* k, unsigned gx, unsigned gy, unsigned gz, unsigned bx,
               unsigned by, unsigned bz, unsigned smem, void** args, int stream);
-/* ad_launch with programmatic dependent launch: the kernel may be scheduled
- * while the previous kernel on the stream finishes; it must execute
- * `griddepcontrol.wait` before touching memory that kernel writes (every
- * generated kernel starts with it).  No reference counterpart. */
-int ad_launch_pdl(ad_ctx* ctx, ad_kernel* k, unsigned gx, unsigned gy, unsigned gz, unsigned bx,
-                  unsigned by, unsigned bz, unsigned smem, void** args, int stream);
 int ad_check(ad_ctx* ctx);
 
 /* TMA descriptor (CUtensorMap, 128 bytes) for a 2-D row-major tensor; used by
