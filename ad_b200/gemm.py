@@ -64,7 +64,7 @@ def plan_dot(dev, cmd, name: str, sizes: Dict[int, int]) -> List[codegen.KernelS
         return [codegen.gen_dot_warp(cmd, name + "_warp", sizes)]
     from . import dot_small
     if use_small_tc(dev, M, N, K):
-        return [dot_small.gen_dot_tc(cmd, name + "_tc", sizes)]
+        return [dot_small.gen_dot_tc(cmd, name + "_small", sizes)]
     return [codegen.gen_dot_simt(cmd, name + "_simt", sizes)]
 
 
