@@ -135,6 +135,7 @@ struct Nccl {
   ncclResult_t (*commDestroy)(ncclComm_t);
   ncclResult_t (*groupStart)();
   ncclResult_t (*groupEnd)();
+  ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
   const char* (*getErrorString)(ncclResult_t);
 };
 Nccl g_nccl;
@@ -161,6 +162,7 @@ int nccl() {
   SYM(commDestroy, "ncclCommDestroy");
   SYM(groupStart, "ncclGroupStart");
   SYM(groupEnd, "ncclGroupEnd");
+  SYM(allGather, "ncclAllGather");
   SYM(getErrorString, "ncclGetErrorString");
 #undef SYM
   g_nccl.ok = true;
@@ -185,6 +187,13 @@ struct ad_ctx {
   std::vector<void*> stage;
   std::vector<cudaEvent_t> stage_ev;
   std::vector<bool> stage_busy;
+  // peer-memory all-reduce (ad_peer_*): this rank's registered region, the
+  // peers' mappings of theirs, barrier flags and the device-side table
+  uint64_t peer_base = 0;
+  size_t peer_bytes = 0;
+  std::vector<void*> peer_maps;       // opened IPC mappings (to close)
+  void* peer_flags = nullptr;         // this rank's flag area (cudaMalloc)
+  void* peer_tab = nullptr;           // device copy of PeerTab
 };
 
 struct ad_kernel {
@@ -362,8 +371,9 @@ int ad_init(int device, int n_streams, ad_ctx** out) {
 int ad_destroy(ad_ctx* c) {
   if (!c) return 0;
   cudaSetDevice(c->device);
-  if (c->comm && g_nccl.ok) g_nccl.commDestroy(c->comm);
   for (auto s : c->streams) cudaStreamSynchronize(s);
+  ad_peer_close(c);
+  if (c->comm && g_nccl.ok) g_nccl.commDestroy(c->comm);
   for (auto e : c->stage_ev) cudaEventDestroy(e);
   for (auto p : c->stage) cudaFreeHost(p);
   for (auto s : c->streams) cudaStreamDestroy(s);
@@ -796,4 +806,186 @@ int ad_nccl_abort(ad_ctx* c) {
   return 0;
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------- peer-memory all-reduce
+// Gradient sums over the GPUs of one node without NCCL: every rank maps every
+// other rank's arena (CUDA IPC over NVLink) and one kernel sums in two shots --
+// rank r adds up shard r of the range from all ranks' copies (in rank order, so
+// every rank gets bit-identical sums) and stores the result into every rank's
+// copy.  Ranks meet at a flag barrier before reading (all gradients written:
+// a rank's kernel runs only after its earlier kernels finished) and after
+// storing (all shards complete before anyone reads its copy, and nobody
+// overwrites a range a slower rank is still reading).  Each block of the kernel
+// meets the same block of the other ranks, so blocks never wait for each other.
+// Every wait is bounded (2 s of %globaltimer): on expiry the kernel records
+// error 7 in the device's error word and returns.
+namespace {
+constexpr int kPeerMaxRanks = 8, kPeerMaxOps = 64, kPeerBlocks = 32, kPeerThreads = 512;
+constexpr size_t kPeerFlagWords = 2ull * kPeerMaxOps * kPeerBlocks * kPeerMaxRanks;
+constexpr size_t kPeerFlagBytes = (kPeerFlagWords + (size_t)kPeerMaxOps * kPeerBlocks) * 4;
+
+struct PeerTab {
+  float* data[kPeerMaxRanks];      // each rank's registered region, as mapped here
+  unsigned* flags[kPeerMaxRanks];  // each rank's flag words, as mapped here
+  unsigned* counters;              // this rank's per-(op, block) epochs
+  int rank, world;
+};
+
+__device__ __forceinline__ void peer_st_release(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned peer_ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long peer_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// thread 0 only: publish `epoch` for (phase, op, block) to every rank, then wait
+// until every rank has published it here
+__device__ bool peer_barrier(const PeerTab& t, int phase, int op, int b, unsigned epoch) {
+  const size_t base = ((size_t)(phase * kPeerMaxOps + op) * kPeerBlocks + b) * kPeerMaxRanks;
+  for (int j = 0; j < t.world; ++j) peer_st_release(t.flags[j] + base + t.rank, epoch);
+  const unsigned* mine = t.flags[t.rank] + base;
+  const unsigned long long t0 = peer_now();
+  for (int j = 0; j < t.world; ++j)
+    while ((int)(peer_ld_acquire(mine + j) - epoch) < 0)
+      if (peer_now() - t0 > 2000000000ull) return false;
+  return true;
+}
+
+__global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const PeerTab* __restrict__ tp,
+                                                                     size_t off, size_t count, int op,
+                                                                     int* err) {
+  __shared__ PeerTab t;
+  __shared__ unsigned epoch;
+  __shared__ int ok;
+  const int b = blockIdx.x;
+  if (threadIdx.x == 0) {
+    t = *tp;
+    unsigned* ctr = t.counters + op * kPeerBlocks + b;
+    epoch = *ctr + 1;
+    *ctr = epoch;
+    ok = peer_barrier(t, 0, op, b, epoch);
+    if (!ok) atomicExch(err, 7);
+  }
+  __syncthreads();
+  if (ok) {
+    const size_t per = ((count + t.world - 1) / t.world + 3) / 4 * 4;
+    const size_t s0 = min(count, (size_t)t.rank * per), s1 = min(count, s0 + per);
+    const size_t chunk = ((s1 - s0 + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
+    const size_t c0 = min(s1, s0 + (size_t)b * chunk), c1 = min(s1, c0 + chunk);
+    for (size_t e = c0 + 4 * (size_t)threadIdx.x; e < c1; e += 4 * (size_t)blockDim.x) {
+      float4 v[kPeerMaxRanks];
+#pragma unroll
+      for (int j = 0; j < kPeerMaxRanks; ++j)
+        if (j < t.world) v[j] = __ldcg(reinterpret_cast<const float4*>(t.data[j] + off + e));  // L2, not a stale L1 line
+      float4 acc = v[0];
+#pragma unroll
+      for (int j = 1; j < kPeerMaxRanks; ++j)
+        if (j < t.world) {
+          acc.x += v[j].x;
+          acc.y += v[j].y;
+          acc.z += v[j].z;
+          acc.w += v[j].w;
+        }
+#pragma unroll
+      for (int j = 0; j < kPeerMaxRanks; ++j)
+        if (j < t.world) __stcg(reinterpret_cast<float4*>(t.data[j] + off + e), acc);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && ok) {
+    __threadfence_system();
+    if (!peer_barrier(t, 1, op, b, epoch)) atomicExch(err, 7);
+  }
+}
+}  // namespace
+
+extern "C" {
+
+int ad_peer_init(ad_ctx* c, uint64_t base, size_t bytes) {
+  if (!c || !c->comm) return fail("ad_peer_init: NCCL communicator not initialised");
+  if (c->world > kPeerMaxRanks) return fail("ad_peer_init: at most %d ranks", kPeerMaxRanks);
+  if (set_dev(c)) return 1;
+  cudaStream_t s = c->streams[0];
+  CK(cudaMalloc(&c->peer_flags, kPeerFlagBytes));
+  CK(cudaMemset(c->peer_flags, 0, kPeerFlagBytes));
+  // exchange (arena handle, flags handle) of every rank with one NCCL all-gather
+  cudaIpcMemHandle_t mine[2];
+  CK(cudaIpcGetMemHandle(&mine[0], reinterpret_cast<void*>(base)));
+  CK(cudaIpcGetMemHandle(&mine[1], c->peer_flags));
+  const size_t hb = sizeof(mine);
+  void* dbuf = nullptr;
+  CK(cudaMalloc(&dbuf, hb * (c->world + 1)));
+  char* send = static_cast<char*>(dbuf) + hb * c->world;
+  CK(cudaMemcpy(send, mine, hb, cudaMemcpyHostToDevice));
+  ncclResult_t r = g_nccl.allGather(send, dbuf, hb, ncclChar, c->comm, s);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    cudaFree(dbuf);
+    return fail("ncclAllGather: %s", g_nccl.getErrorString(r));
+  }
+  if (nccl_wait(c, "ncclAllGather")) { cudaFree(dbuf); return 1; }
+  std::vector<cudaIpcMemHandle_t> all(2 * c->world);
+  CK(cudaStreamSynchronize(s));
+  CK(cudaMemcpy(all.data(), dbuf, hb * c->world, cudaMemcpyDeviceToHost));
+  CK(cudaFree(dbuf));
+  PeerTab tab{};
+  for (int j = 0; j < c->world; ++j) {
+    if (j == c->rank) {
+      tab.data[j] = reinterpret_cast<float*>(base);
+      tab.flags[j] = static_cast<unsigned*>(c->peer_flags);
+      continue;
+    }
+    void* pd = nullptr;
+    void* pf = nullptr;
+    CK(cudaIpcOpenMemHandle(&pd, all[2 * j], cudaIpcMemLazyEnablePeerAccess));
+    c->peer_maps.push_back(pd);
+    CK(cudaIpcOpenMemHandle(&pf, all[2 * j + 1], cudaIpcMemLazyEnablePeerAccess));
+    c->peer_maps.push_back(pf);
+    tab.data[j] = static_cast<float*>(pd);
+    tab.flags[j] = static_cast<unsigned*>(pf);
+  }
+  tab.counters = static_cast<unsigned*>(c->peer_flags) + kPeerFlagWords;
+  tab.rank = c->rank;
+  tab.world = c->world;
+  CK(cudaMalloc(&c->peer_tab, sizeof(PeerTab)));
+  CK(cudaMemcpy(c->peer_tab, &tab, sizeof(PeerTab), cudaMemcpyHostToDevice));
+  c->peer_base = base;
+  c->peer_bytes = bytes;
+  return 0;
+}
+
+int ad_peer_allreduce_f32(ad_ctx* c, uint64_t ptr, size_t count, int op, int stream, uint64_t err) {
+  cudaStream_t s;
+  if (stream_of(c, stream, &s)) return 1;
+  if (!c->peer_tab) return fail("ad_peer_allreduce_f32: ad_peer_init was not called");
+  if (op < 0 || op >= kPeerMaxOps) return fail("ad_peer_allreduce_f32: op slot %d outside [0, %d)", op, kPeerMaxOps);
+  if (ptr < c->peer_base || ptr + 4 * count > c->peer_base + c->peer_bytes)
+    return fail("ad_peer_allreduce_f32: range outside the registered region");
+  if ((ptr - c->peer_base) % 16 || count % 4) return fail("ad_peer_allreduce_f32: range must be 16-byte aligned");
+  peer_allreduce_kernel<<<kPeerBlocks, kPeerThreads, 0, s>>>(static_cast<const PeerTab*>(c->peer_tab),
+                                                           (ptr - c->peer_base) / 4, count, op,
+                                                           reinterpret_cast<int*>(err));
+  CK(cudaGetLastError());
+  return 0;
+}
+
+int ad_peer_close(ad_ctx* c) {
+  if (!c) return 0;
+  cudaSetDevice(c->device);
+  for (void* p : c->peer_maps) cudaIpcCloseMemHandle(p);
+  c->peer_maps.clear();
+  if (c->peer_tab) cudaFree(c->peer_tab);
+  if (c->peer_flags) cudaFree(c->peer_flags);
+  c->peer_tab = c->peer_flags = nullptr;
+  c->peer_base = 0;
+  c->peer_bytes = 0;
+  return 0;
+}
 }  // extern "C"

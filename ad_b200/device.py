@@ -105,6 +105,8 @@ class CudaB200Device:
         # ranks then diverge)
         self.comm_trace = None
         self.skip_comm = os.environ.get("AD_DP_SKIP_COMM", "0") == "1"
+        # gradient sums: NCCL, or the library's peer-memory kernel (AD_DP_COMM=peer)
+        self.peer_comm = os.environ.get("AD_DP_COMM", "nccl") == "peer"
 
     # ------------------------------------------------------------ memory
     def ptr(self, buf_id: int) -> int:
@@ -216,6 +218,8 @@ class CudaB200Device:
                 if off < 0 or off + n > self.slots[k.id].size:
                     raise ValueError(f"{kind} access out of range for buffer {k.id}")
             return
+        if kind == "AllReduce":
+            self._comm_slot[id(cmd)] = len(self._comm_slot)
         if kind == "AllReduce" and cmd.async_start:
             # fork/join events of the communication stream (recorded again by
             # every replay; inside a graph capture they become dependencies)
@@ -306,7 +310,12 @@ class CudaB200Device:
             if trace is not None:
                 t0, t1 = self.ctx.event(True), self.ctx.event(True)
                 t0.record(stream)
-            if not self.skip_comm:
+            if self.skip_comm:
+                pass
+            elif self.peer_comm:
+                rt.check(self.ctx.L.ad_peer_allreduce_f32(self.ctx.h, p, cmd.count, self._comm_slot[id(cmd)],
+                                                          stream, self.err_ptr), "ad_peer_allreduce_f32")
+            else:
                 rt.check(self.ctx.L.ad_allreduce_f32(self.ctx.h, p, p, cmd.count, 0, stream),
                          "ad_allreduce_f32")
             if trace is not None:
@@ -433,6 +442,9 @@ class CudaB200Device:
         gemm.setup_scratch(self, proc)
         self._pending = []
         self._comm_events = {}
+        self._comm_slot = {}
+        if self.world > 1 and self.peer_comm:
+            rt.check(self.ctx.L.ad_peer_init(self.ctx.h, self.arena, self.arena_bytes), "ad_peer_init")
         self._run_proc(proc, self.init, init=True)
         self._compile_pending()
         return proc

@@ -125,6 +125,22 @@ int ad_allreduce_f32(ad_ctx* ctx, uint64_t send, uint64_t recv, size_t count, in
                      int stream);
 int ad_nccl_abort(ad_ctx* ctx);
 
+/* Gradient all-reduce over peer memory (no reference counterpart: the
+ * reference has no multi-device code).  ad_peer_init maps every rank's
+ * registered region (one cudaMalloc allocation starting at `base`: the
+ * device's arena) into every other rank over CUDA IPC, exchanging the handles
+ * with one NCCL all-gather (call it on all ranks after ad_nccl_init).
+ * ad_peer_allreduce_f32 sums `count` floats at `ptr` (inside the region,
+ * 16-byte aligned, count % 4 == 0) over all ranks in place with one kernel:
+ * reduce-scatter + all-gather through NVLink loads and stores, ranks meeting
+ * at flag barriers.  `op` (0..63) names the call site: each site's calls must
+ * come in the same order on every rank.  A barrier that waits more than 2 s
+ * writes 7 to the int at `err` (device address) and the kernel returns.
+ * ad_peer_close unmaps (also done by ad_destroy). */
+int ad_peer_init(ad_ctx* ctx, uint64_t base, size_t bytes);
+int ad_peer_allreduce_f32(ad_ctx* ctx, uint64_t ptr, size_t count, int op, int stream, uint64_t err);
+int ad_peer_close(ad_ctx* ctx);
+
 /* C = A @ B (b_is_nk = 0: B is K x N row-major) or C = A @ B^T (b_is_nk = 1:
  * B is N x K row-major); A is M x K row-major, C is M x N row-major, all fp32
  * device pointers; 3xTF32 on tcgen05.  No counterpart in the reference: this

@@ -22,9 +22,10 @@ def _free_port():
     return port
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, comm="nccl"):
     import torch.distributed as td
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      AD_DP_COMM=comm)
     td.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from ad_b200 import dist
@@ -43,7 +44,9 @@ def _rank(rank, world, port, q):
         td.destroy_process_group()
 
 
-def test_two_gpu_data_parallel_matches_full_batch():
+@pytest.mark.parametrize("comm", ["nccl", "peer"])
+def test_two_gpu_data_parallel_matches_full_batch(comm):
+    """``peer``: the library's own all-reduce kernel over CUDA IPC mappings."""
     from ad_b200 import runtime as rt
     if rt.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -56,7 +59,7 @@ def test_two_gpu_data_parallel_matches_full_batch():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, comm)) for r in range(2)]
     for pr in procs:
         pr.start()
     res = dict(q.get(timeout=600) for _ in range(2))
@@ -66,3 +69,5 @@ def test_two_gpu_data_parallel_matches_full_batch():
         assert not isinstance(res[r], str), res[r]
         for g, w in zip(res[r], o.last_received):
             np.testing.assert_allclose(g, w, rtol=1e-3, atol=1e-4)
+    for g0, g1 in zip(res[0], res[1]):
+        np.testing.assert_array_equal(g0, g1)        # every rank holds the same parameters
