@@ -821,7 +821,7 @@ int ad_nccl_abort(ad_ctx* c) {
 // Every wait is bounded (2 s of %globaltimer): on expiry the kernel records
 // error 7 in the device's error word and returns.
 namespace {
-constexpr int kPeerMaxRanks = 8, kPeerMaxOps = 64, kPeerBlocks = 32, kPeerThreads = 512;
+constexpr int kPeerMaxRanks = 8, kPeerMaxOps = 64, kPeerBlocks = 128, kPeerThreads = 512, kPeerUnroll = 4;
 constexpr size_t kPeerFlagWords = 2ull * kPeerMaxOps * kPeerBlocks * kPeerMaxRanks;
 constexpr size_t kPeerFlagBytes = (kPeerFlagWords + (size_t)kPeerMaxOps * kPeerBlocks) * 4;
 
@@ -880,23 +880,39 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const Peer
     const size_t s0 = min(count, (size_t)t.rank * per), s1 = min(count, s0 + per);
     const size_t chunk = ((s1 - s0 + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
     const size_t c0 = min(s1, s0 + (size_t)b * chunk), c1 = min(s1, c0 + chunk);
-    for (size_t e = c0 + 4 * (size_t)threadIdx.x; e < c1; e += 4 * (size_t)blockDim.x) {
-      float4 v[kPeerMaxRanks];
+    // kPeerUnroll float4 per thread per sweep, loads of every rank issued before the adds,
+    // so each thread keeps several NVLink reads in flight
+    const size_t step = 4 * (size_t)blockDim.x;
+    for (size_t e0 = c0 + 4 * (size_t)threadIdx.x; e0 < c1; e0 += step * kPeerUnroll) {
+      float4 acc[kPeerUnroll];
 #pragma unroll
-      for (int j = 0; j < kPeerMaxRanks; ++j)
-        if (j < t.world) v[j] = __ldcg(reinterpret_cast<const float4*>(t.data[j] + off + e));  // L2, not a stale L1 line
-      float4 acc = v[0];
+      for (int u = 0; u < kPeerUnroll; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int j = 1; j < kPeerMaxRanks; ++j)
-        if (j < t.world) {
-          acc.x += v[j].x;
-          acc.y += v[j].y;
-          acc.z += v[j].z;
-          acc.w += v[j].w;
+      for (int j = 0; j < kPeerMaxRanks; ++j) {
+        if (j >= t.world) break;
+        float4 v[kPeerUnroll] = {};
+#pragma unroll
+        for (int u = 0; u < kPeerUnroll; ++u) {
+          const size_t e = e0 + u * step;
+          if (e < c1) v[u] = __ldcg(reinterpret_cast<const float4*>(t.data[j] + off + e));  // L2, not a stale L1 line
         }
 #pragma unroll
-      for (int j = 0; j < kPeerMaxRanks; ++j)
-        if (j < t.world) __stcg(reinterpret_cast<float4*>(t.data[j] + off + e), acc);
+        for (int u = 0; u < kPeerUnroll; ++u) {   // rank order: the same sums on every rank
+          acc[u].x += v[u].x;
+          acc[u].y += v[u].y;
+          acc[u].z += v[u].z;
+          acc[u].w += v[u].w;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kPeerMaxRanks; ++j) {
+        if (j >= t.world) break;
+#pragma unroll
+        for (int u = 0; u < kPeerUnroll; ++u) {
+          const size_t e = e0 + u * step;
+          if (e < c1) __stcg(reinterpret_cast<float4*>(t.data[j] + off + e), acc[u]);
+        }
+      }
     }
   }
   __syncthreads();

@@ -297,8 +297,9 @@ def build_parser():
 def main():
     args = build_parser().parse_args()
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-        # NCCL's init lines name the communicator's rank count and its algorithms (NVLS)
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        # NCCL's init lines name the communicator's rank count and its algorithms (NVLS);
+        # set outright: an inherited NCCL_DEBUG=VERSION would hide them
+        os.environ["NCCL_DEBUG"] = "INFO"
     args.warmup = max(args.warmup, 3)
     wl = WORKLOADS[args.workload]
     rank, world, local = dist_env()
@@ -532,11 +533,12 @@ def bench_loop(args, wl, rank, world, local, td):
                                        else f"replicas x{world}")},
             "gpu_launches": len(launches) * args.steps,
             "roofline": roof,
-            "per_kernel_ms": [round(float(x), 4) for x in per_kernel],
-            "per_kernel_kind": [L.spec.kind for L in launches],
-            "per_kernel_gflop": [round(L.spec.flops / 1e9, 3) for L in launches],
-            "per_kernel_GBps": [round(L.spec.bytes_moved / (t / 1e3) / 1e9, 1) if t > 0 else None
-                                for L, t in zip(launches, per_kernel)],
+            **({} if not timed else {
+                "per_kernel_ms": [round(float(x), 4) for x in per_kernel],
+                "per_kernel_kind": [L.spec.kind for L in launches],
+                "per_kernel_gflop": [round(L.spec.flops / 1e9, 3) for L in launches],
+                "per_kernel_GBps": [round(L.spec.bytes_moved / (t / 1e3) / 1e9, 1) if t > 0 else None
+                                    for L, t in zip(launches, per_kernel)]}),
             "clocks": clk.summary(),
             "comm_profile": comm,
             "e2e": {"value": (value * ms / e2e["ms_per_step"]), "unit": wl["unit"],
