@@ -291,7 +291,8 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
     unsigned long long* empty = full + STAGES;
     unsigned long long* tfull = empty + STAGES;
     unsigned long long* tempty = tfull + 2;
-    unsigned* tmem_slot = (unsigned*)(tempty + 2);
+    unsigned long long* drain = tempty + 2;                                   // abort path only
+    unsigned* tmem_slot = (unsigned*)(drain + 1);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
     volatile int* consumed = abort_flag + 1;
 
@@ -300,6 +301,7 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], EPI_WARPS); }
+        mbar_init(drain, 1);
         *abort_flag = 0;
         *consumed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -390,6 +392,13 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
                 }
                 if (!ok) break;
                 mma_commit(&tfull[a]);
+            }
+            if (*abort_flag && it > 0) {
+                // MMAs already issued may still be running: let them finish (bounded)
+                // before the block frees its TMEM
+                mma_commit(drain);
+                const unsigned long long t0 = gtime();
+                while (!mbar_try(drain, 0) && gtime() - t0 < AD_WAIT_NS) {}
             }
         }
     } else {
