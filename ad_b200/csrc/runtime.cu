@@ -19,6 +19,7 @@
 // NCCL is dlopen'ed on first use.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cuda_profiler_api.h>
 #include <nvrtc.h>
 #include <nccl.h>
 #include <dlfcn.h>
@@ -1004,4 +1005,9 @@ int ad_peer_close(ad_ctx* c) {
   c->peer_bytes = 0;
   return 0;
 }
+int ad_profiler_range(int on) {
+  CK(on ? cudaProfilerStart() : cudaProfilerStop());
+  return 0;
+}
+
 }  // extern "C"

@@ -72,6 +72,7 @@ SIGNATURES = {
     "ad_peer_init": (c_int, [c_void_p, c_u64, c_size_t]),
     "ad_peer_allreduce_f32": (c_int, [c_void_p, c_u64, c_size_t, c_int, c_int, c_u64]),
     "ad_peer_close": (c_int, [c_void_p]),
+    "ad_profiler_range": (c_int, [c_int]),
     "ad_dot_tf32x3_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
 }
 

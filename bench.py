@@ -55,6 +55,7 @@ WORKLOADS = {
             "unit": "steps/s", "loop": True, "cpu_iters": 1, "dp": True, "global_batch": 32,
             "data": "synthetic: x ~ N(0,1) [4096, 512] seed 0 via Feeder; Xavier-uniform weights (seeded)"},
     "enc_weak": {"case": "enc_4_32_128_512_8_2048_100",
+                 "profile": ("gemm_tcgen05", "gemm_tcgen05_enc_4l_b32_top.md"),
                  "metric": "encoder train sequences/s (config 4: 4 layers, d512, 8 heads, ff2048, S128, batch 32 per GPU, fp32, SGD; data parallel over N GPUs)",
                  "unit": "sequences/s", "loop": True, "cpu_iters": 1, "dp": "weak", "batch_per_gpu": 32,
                  "data": "synthetic: x ~ N(0,1) [4096, 512] per rank (seed 1000*rank) via Feeder; Xavier-uniform weights (seeded, same on every rank)"},
@@ -494,6 +495,8 @@ def bench_loop(args, wl, rank, world, local, td):
     hbm, bf16, peak_kind = peaks()
     kt = max(per_kernel[top], 1e-9) / 1e3
     timed = not args.no_kernel_timing
+    if timed and os.environ.get("AD_PROFILE_TOP") == "1":
+        profile_one(dev, Lt)
     if Lt.spec.kind == "gemm_tcgen05" and not args.no_kernel_timing:
         from ad_b200 import tcgen05
         tf32 = tcgen05.measure_tf32_peak(ctx, dev.err_ptr)
@@ -506,8 +509,10 @@ def bench_loop(args, wl, rank, world, local, td):
         achieved = Lt.spec.bytes_moved / kt / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "traffic": None, "peak_kind": peak_kind}
+    traffic, traffic_src = profile_traffic(wl, Lt.spec.kind)
     roof.update({"kernel": f"{top}:{Lt.spec.kind}", "kernel_ms": float(per_kernel[top]),
-                 "alg_bytes": Lt.spec.bytes_moved})
+                 "alg_bytes": Lt.spec.bytes_moved, "traffic": traffic, "traffic_source": traffic_src,
+                 "gflop": round(Lt.spec.flops / 1e9, 3)})
     if not timed:
         roof = None                     # --no-kernel-timing: no per-kernel figures
     work_set = dev.arena_bytes + getattr(dev, "scratch_bytes", 0)
@@ -555,6 +560,17 @@ def bench_loop(args, wl, rank, world, local, td):
         print(json.dumps(line), flush=True)
     dev.close()
     barrier(td)
+
+
+def profile_one(dev, L):
+    """One launch of ``L`` inside a profiler range (``ncu --profile-from-start off``
+    then captures exactly this launch of the dominant kernel)."""
+    from ad_b200 import runtime as rt
+    dev.ctx.sync()
+    rt.check(rt.lib().ad_profiler_range(1), "ad_profiler_range")
+    dev._launch(L)
+    dev.ctx.sync()
+    rt.check(rt.lib().ad_profiler_range(0), "ad_profiler_range")
 
 
 def comm_profile(dev, loop, td):

@@ -141,6 +141,11 @@ int ad_peer_init(ad_ctx* ctx, uint64_t base, size_t bytes);
 int ad_peer_allreduce_f32(ad_ctx* ctx, uint64_t ptr, size_t count, int op, int stream, uint64_t err);
 int ad_peer_close(ad_ctx* ctx);
 
+/* cudaProfilerStart (on != 0) / cudaProfilerStop: brackets the launches a
+ * profiler started with "--profile-from-start off" captures.  No reference
+ * counterpart (measurement only). */
+int ad_profiler_range(int on);
+
 /* C = A @ B (b_is_nk = 0: B is K x N row-major) or C = A @ B^T (b_is_nk = 1:
  * B is N x K row-major); A is M x K row-major, C is M x N row-major, all fp32
  * device pointers; 3xTF32 on tcgen05.  No counterpart in the reference: this
