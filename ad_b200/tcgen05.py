@@ -117,7 +117,60 @@ def _gen_split(karg: ir.KernelArg, name: str, rows: int, kdim: int, rows_p: int,
         (lambda ga, gb: {row_var: ga, k_var: gb})
     other_ext = rows if orient == "k" else kdim
 
+    def uniform_cond(cond) -> bool:
+        """Whether a concatenation's condition has one value over the four
+        lanes of a float4 (``ga`` is a multiple of 4)."""
+        gc = codegen._gt_const(cond)
+        if gc is not None and exprs._var(gc[0]) == lane_var:
+            t = gc[1]
+            return float(t) == int(t) and (int(t) + 1) % 4 == 0
+        return exprs.lanes(cond, lane_var, 4, {other: 1}).s == 0
+
+    def tree4(k, dst: str, ga: str, gb: str, env0) -> List[str]:
+        """Four lane values of ``k`` into ``dst``: a concatenation whose
+        condition is the same for the four lanes branches once and reads the
+        chosen piece (the piece the per-element conditionals select), a plain
+        unit-stride piece with one 16-byte load."""
+        if isinstance(k, ir.KConcat) and uniform_cond(k.condition):
+            cp = codegen.concat_pieces(k)
+            if cp is not None and all(uniform_cond(ir.Bin("MoreThan", cp[0], ir.Const(t))) for t in cp[2][1:]):
+                # a chain of pieces along one axis: binary search over the thresholds
+                v, parts, ths = cp
+
+                def search(lo: int, hi: int) -> List[str]:
+                    if hi - lo == 1:
+                        return tree4(parts[lo], dst, ga, gb, env0)
+                    mid = (lo + hi) // 2
+                    return ([f"if ({em.expr(v, env0)} > ({it}){ths[mid]}) {{"] +
+                            ["    " + x for x in search(mid, hi)] + ["} else {"] +
+                            ["    " + x for x in search(lo, mid)] + ["}"])
+                return search(0, len(parts))
+            return ([f"if ({em.expr(k.condition, env0)} != 0) {{"] +
+                    ["    " + x for x in tree4(k.karg_two, dst, ga, gb, env0)] + ["} else {"] +
+                    ["    " + x for x in tree4(k.karg_one, dst, ga, gb, env0)] + ["}"])
+        out = []
+        kvec = isinstance(k, ir.KMatrix) and not k.is_temp and \
+            exprs.lanes(k.access, lane_var, 4, {other: 1}).unit(4)
+        if kvec:
+            out.append(f"if ({ga} + 3 < ({it}){extent}) {dst} = "
+                       f"*reinterpret_cast<const float4*>(&{em.at(k, env0)});")
+            out.append("else {")
+        else:
+            out.append("{")
+        for j, comp in enumerate("xyzw"):
+            envj = dict(coords(f"({ga} + {j})", gb), G=f"(({it})0)")
+            out.append(f"    if ({ga} + {j} < ({it}){extent}) {dst}.{comp} = {em.scalar_karg(k, envj, {})};")
+        out.append("}")
+        return out
+
     def load4(dst: str, ga: str, gb: str) -> str:
+        if not plain and isinstance(karg, ir.KConcat) and uniform_cond(karg.condition):
+            env0 = dict(coords(ga, gb), G=f"(({it})0)")
+            lines = [f"float4 {dst} = make_float4(0.0f, 0.0f, 0.0f, 0.0f);",
+                     f"if ({gb} < ({it}){other_ext}) {{"]
+            lines += ["    " + x for x in tree4(karg, dst, ga, gb, env0)]
+            lines.append("}")
+            return "\n        ".join(lines)
         env0 = dict(coords(ga, gb), G=f"(({it})0)")
         lines = [f"float4 {dst} = make_float4(0.0f, 0.0f, 0.0f, 0.0f);",
                  f"if ({gb} < ({it}){other_ext}) {{"]
@@ -721,6 +774,8 @@ class GroupPlan:
             self.bn = bn0
             units = n * mblk * (self.Np // bn0)
         self.ks = choose_ksplit(units, self.Kp // BKF, sm_count, self.bn)
+        if os.environ.get("AD_GEMM_KSPLIT"):       # forced K slices (accuracy / tuning studies)
+            self.ks = max(1, min(int(os.environ["AD_GEMM_KSPLIT"]), self.Kp // BKF))
         self.raw = self.ks > 1 or heavy_epilogue(cmds[0], n, units, self.Kp // BKF, sm_count)
 
     def _dedupe(self, cmds, which: int, name: str):
