@@ -486,13 +486,17 @@ class CudaB200Device:
 
     def transform(self, proc) -> ir.Proc:
         """Command-level passes: a private copy of the proc, then the gradient
-        all-reduce rewrite (data parallel), splitting of horizontally fused
+        all-reduce rewrite (data parallel), sums of dot products folded into
+        one dot over the concatenated K axis, splitting of horizontally fused
         elementwise groups, row fusion, and batching."""
         proc = ir.copy_structure(ir.conv_proc(proc))
         if self.world > 1 or os.environ.get("AD_DP_FORCE_REWRITE") == "1":
             # (forced on one GPU with AD_DP_SKIP_COMM=1: profiles the rewrite's own cost)
             from . import dist
             dist.insert_grad_allreduce(proc)
+        if os.environ.get("AD_KCAT", "1") != "0":
+            from . import kcat
+            kcat.fuse_ksums(proc)
         if self.hsplit:
             from . import hsplit
             hsplit.split_groups(proc)

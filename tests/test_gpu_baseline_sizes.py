@@ -112,7 +112,7 @@ def test_encoder_4_layers_batch32_one_step():
 
 def test_encoder_4_layers_three_steps():
     """4 layers at config 4's layer shapes, batch 8, loss = sum(out * R) with a
-    fixed R ~ N(0,1): every parameter after three SGD steps, rel 1e-3."""
-    got, want, _ = both("encdy_4_8_128_512_8_2048_3", loops=3)
-    for g, w in zip(got, want):
-        np.testing.assert_allclose(g, w, rtol=1e-3, atol=1e-4)
+    fixed R ~ N(0,1), lr 1e-4 (at 0.01 this batch diverges within the first
+    step): every parameter and every update after three SGD steps."""
+    from tests.test_gpu_parity import assert_sgd_parity
+    assert_sgd_parity("encdy_4_8_128_512_8_2048_3_lr4", 3)

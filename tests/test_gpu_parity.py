@@ -259,11 +259,32 @@ def test_encoder_layer_sgd_step():
         np.testing.assert_allclose(g, w, rtol=1e-3, atol=1e-4)
 
 
-@pytest.mark.parametrize("batch,gemm", [(True, "auto"), (False, "auto"), (True, "tc")])
-def test_encoder_layer_sgd_steps_well_conditioned(batch, gemm):
-    """Same layer with loss = sum(out * R), R ~ N(0,1) fixed: parameters after 3 SGD
-    steps vs the oracle, rel 1e-3 (batched attention kernels, row-fused
-    LayerNorm/softmax, tensor-core FFN, CUDA-graph loop replay)."""
-    got, want, _ = both("encdy_1_8_128_512_8_2048_3", loops=3, batch=batch, gemm=gemm)
+def assert_sgd_parity(case, loops, **devkw):
+    """Parameters after ``loops`` SGD steps vs the oracle: every parameter
+    within rel 1e-3 / abs 1e-4, and every update ``p - p0`` within rel 1e-2 of
+    the oracle's update (or at least as close to the float64 update), so a
+    wrong update cannot hide behind the size of the unchanged weight.  The
+    oracle's values must be finite (a diverging fixture compares nothing)."""
+    from ad_b200 import ir
+    from ad_b200.device import offset_of
+    got, want, _ = both(case, loops=loops, **devkw)
+    assert all(np.isfinite(w).all() for w in want)
     for g, w in zip(got, want):
         np.testing.assert_allclose(g, w, rtol=1e-3, atol=1e-4)
+    p, _ = load_case(case)
+    init = {c.id: np.asarray(c.content, np.float32).reshape(-1) for c in ir.iter_cmds(p)
+            if type(c).__name__ == "AllocEntry" and c.content is not None}
+    rec = next(c for c in ir.iter_cmds(p) if type(c).__name__ == "Receiver")
+    p0 = [init[k.id][offset_of(k):offset_of(k) + g.size].reshape(g.shape) for k, g in zip(rec.kargs, got)]
+    exact = exact_of(case, loops=loops)
+    assert_parity([g - a for g, a in zip(got, p0)], [w - a for w, a in zip(want, p0)],
+                  [e - a for e, a in zip(exact, p0)], rtol=1e-2, atol=1e-6)
+
+
+@pytest.mark.parametrize("batch,gemm", [(True, "auto"), (False, "auto"), (True, "tc")])
+def test_encoder_layer_sgd_steps_well_conditioned(batch, gemm):
+    """Same layer with loss = sum(out * R), R ~ N(0,1) fixed, lr 1e-4 (at the
+    reference's 0.01 this batch diverges within the first step): 3 SGD steps
+    (batched attention kernels, row-fused LayerNorm/softmax, tensor-core FFN,
+    CUDA-graph loop replay)."""
+    assert_sgd_parity("encdy_1_8_128_512_8_2048_3_lr4", 3, batch=batch, gemm=gemm)
