@@ -45,6 +45,15 @@ BN_DEFAULT = 256
 # fp32 of K per stage row: 16 (64-byte rows, SWIZZLE_64B) or 32 (128-byte rows, SWIZZLE_128B)
 BKF = int(os.environ.get("AD_GEMM_BK", "16"))
 GROUP_M = int(os.environ.get("AD_GEMM_GROUP", "16"))
+# K blocks accumulated in TMEM before the epilogue warps add them into fp32 running
+# sums (0: the whole K slice in one TMEM accumulator).  The tensor core's fp32
+# accumulation truncates (a bias toward zero of ~0.4 ulp per MMA accumulate), so
+# the error of a product grows with the K it accumulates in one place.
+# Off by default: measured on the config-4 step it costs 29% (4.74 vs 3.67 ms at 4 K blocks).
+
+
+def fold_kb() -> int:
+    return int(os.environ.get("AD_GEMM_FOLD", "0"))
 SMEM_STAGES_BYTES = 192 * 1024
 
 
@@ -309,6 +318,27 @@ __device__ __forceinline__ void mma_tf32(unsigned tmem, unsigned long long ad, u
                  " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}"
                  :: "r"(tmem), "l"(ad), "l"(bd), "r"(idesc), "r"(acc) : "memory");
 }
+__device__ __forceinline__ void tmem_ld32(unsigned taddr, unsigned (&r)[32]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st32(unsigned taddr, const unsigned (&r)[32]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+           "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+           "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+           "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
 __device__ __forceinline__ void mma_commit(unsigned long long* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(smem_u32(bar)) : "memory");
 }
@@ -402,6 +432,7 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
                 }
             }
         }
+#if AD_FOLD == 0
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer: D(128 x BN) += A(128 x 8) * B(BN x 8)^T, K-major, 3xTF32
@@ -510,6 +541,145 @@ extern "C" __global__ void __launch_bounds__(320, 1) NAME(
             }
         }
     }
+#else
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer, folded accumulation: every AD_FOLD K blocks the
+            // chunk accumulator (TMEM columns [0, BN)) is handed to the epilogue warps, which
+            // add it into fp32 running sums (columns [BN, 2 BN)) on the CUDA cores
+            constexpr unsigned IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((unsigned)(BN >> 3) << 17) | ((128u >> 4) << 24);
+            int it = 0, gc = 0;
+            for (int t = blockIdx.x; t < NUM_TILES && !*abort_flag; t += gridDim.x) {
+                bool ok = true;
+                int inst, ks, mb, nb;
+                decode(t, inst, ks, mb, nb);
+                const int kb0 = ks * KB / KSPLIT, kb1 = (ks + 1) * KB / KSPLIT;
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    const bool cstart = ((kb - kb0) % AD_FOLD) == 0;
+                    if (cstart && gc > 0) {
+                        // the previous chunk has been read out of the accumulator
+                        if (!mbar_wait(&tempty[0], (gc - 1) & 1, abort_flag)) {
+                            if (!*abort_flag) atomicExch(err, 4);
+                            *abort_flag = 1;
+                            ok = false;
+                            break;
+                        }
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    }
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&full[s], (it / STAGES) & 1, abort_flag)) {
+                        if (!*abort_flag) atomicExch(err, 2);
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    unsigned char* st = smem + s * STAGE_BYTES;
+                    const unsigned long long ah = sdesc(st), al = sdesc(st + A_BYTES);
+                    const unsigned long long bh = sdesc(st + 2 * A_BYTES), bl = sdesc(st + 2 * A_BYTES + B_BYTES);
+                    #pragma unroll
+                    for (int k8 = 0; k8 < BKF / 8; ++k8) {
+                        const unsigned long long adv = (unsigned long long)(k8 * 32) >> 4;  // 8 fp32 = 32 bytes
+                        const unsigned first = (!cstart || k8 > 0) ? 1u : 0u;
+                        mma_tf32(tmem, ah + adv, bh + adv, IDESC, first);
+                        mma_tf32(tmem, ah + adv, bl + adv, IDESC, 1u);
+                        mma_tf32(tmem, al + adv, bh + adv, IDESC, 1u);
+                    }
+                    mma_commit(&empty[s]);
+                    *consumed = it + 1;
+                    if ((kb + 1 - kb0) % AD_FOLD == 0 || kb + 1 == kb1) {
+                        mma_commit(&tfull[0]);
+                        ++gc;
+                    }
+                }
+                if (!ok) break;
+            }
+            if (*abort_flag && it > 0) {
+                // MMAs already issued may still be running: let them finish (bounded)
+                // before the block frees its TMEM
+                mma_commit(drain);
+                const unsigned long long t0 = gtime();
+                while (!mbar_try(drain, 0) && gtime() - t0 < AD_WAIT_NS) {}
+            }
+        }
+    } else {
+        // ---------------- epilogue warps, folded accumulation
+        const int q = warp & 3;                 // TMEM lane quarter this warp may access
+        const int half = (warp - 2) >> 2;       // which half of the BN columns
+        float* tr = trans + (warp - 2) * 1024;
+        int egc = 0;
+        bool live = true;
+        for (int t = blockIdx.x; t < NUM_TILES && live; t += gridDim.x) {
+            int inst, ks, mb, nb;
+            decode(t, inst, ks, mb, nb);
+            const int kb0 = ks * KB / KSPLIT, kb1 = (ks + 1) * KB / KSPLIT;
+            const int nch = (kb1 - kb0 + AD_FOLD - 1) / AD_FOLD;
+            const int m0 = mb * 128, n0 = nb * BN;
+            const unsigned lanes = (unsigned)(q * 32) << 16;
+            for (int ch = 0; ch < nch; ++ch, ++egc) {
+                if (!mbar_wait(&tfull[0], egc & 1, abort_flag)) {
+                    if (lane == 0 && !*abort_flag) atomicExch(err, 3);
+                    *abort_flag = 1;
+                    live = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                if (ch + 1 < nch) {
+                    // fold this chunk into the running sums: sum = (ch ? sum : 0) + chunk
+                    #pragma unroll 1
+                    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+                        unsigned r[32], u[32];
+                        tmem_ld32(tmem + lanes + (unsigned)(c * 32), r);
+                        if (ch > 0) {
+                            tmem_ld32(tmem + lanes + (unsigned)(BN + c * 32), u);
+                            #pragma unroll
+                            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(u[j]) + __uint_as_float(r[j]));
+                        }
+                        tmem_st32(tmem + lanes + (unsigned)(BN + c * 32), r);
+                    }
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[0]);
+                    continue;
+                }
+                // last chunk of the tile: sum + chunk, then the tile's epilogue
+                EPI_PTRS
+                #pragma unroll 1
+                for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+                    unsigned r[32];
+                    tmem_ld32(tmem + lanes + (unsigned)(c * 32), r);
+                    if (nch > 1) {
+                        unsigned u[32];
+                        tmem_ld32(tmem + lanes + (unsigned)(BN + c * 32), u);
+                        #pragma unroll
+                        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(u[j]) + __uint_as_float(r[j]));
+                    }
+                    if (c == (half + 1) * (BN / 64) - 1) {
+                        // last TMEM read of this chunk by this warp: hand the accumulator back
+                        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[0]);
+                    }
+                    #pragma unroll
+                    for (int j = 0; j < 32; ++j) tr[lane * 32 + (j ^ lane)] = __uint_as_float(r[j]);
+                    __syncwarp();
+                    CHUNK_SETUP
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const IDX om = (IDX)m0 + q * 32 + i;
+                        const IDX on = ON_BASE + lane;
+                        if (CHUNK_OK && om < (IDX)M_DIM && on < (IDX)N_DIM) {
+                            const float accv = tr[i * 32 + (lane ^ i)];
+                            EPILOGUE
+                        }
+                    }
+                    __syncwarp();
+                }
+            }
+        }
+    }
+#endif
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0) {
@@ -646,7 +816,8 @@ def gen_gemm(c, name: str, M: int, N: int, K: int, bn: int, stages: int, sm_coun
            .replace("A_ROW", a_row).replace("B_ROW", b_row).replace("EPI_PTRS", epi_ptrs)
            .replace("CHUNK_SETUP", chunk_setup).replace("ON_BASE", on_base).replace("CHUNK_OK", chunk_ok)
            .replace("M_BLOCKS", str(mblk)).replace("N_BLOCKS", str(nblk_plain))
-           .replace("IDX", it).replace("M_DIM", str(M)).replace("N_DIM", str(N)).replace("EPILOGUE", epi))
+           .replace("IDX", it).replace("M_DIM", str(M)).replace("N_DIM", str(N)).replace("EPILOGUE", epi)
+           .replace("AD_FOLD", str(fold_kb())))
     stage_bytes = 2 * 128 * BKF * 4 + 2 * bn * BKF * 4
     smem = stages * stage_bytes + 8 * 4096 + 1024 + 256
     grid = (min(total, sm_count), 1, 1)

@@ -78,3 +78,22 @@ def test_small_dot_epilogue_bias_scale():
     want = (A.astype(np.float64) @ B + b) * -0.5
     mag = (np.abs(A).astype(np.float64) @ np.abs(B) + np.abs(b)) * 0.5
     assert np.all(np.abs(got - want) <= 1e-4 * mag + 1e-5)
+
+
+def test_folded_accumulation_bias(monkeypatch):
+    """``AD_GEMM_FOLD=4``: the TMEM accumulator is added into fp32 running sums
+    every 4 K blocks (64 of K).  The tensor core's fp32 accumulation truncates,
+    so on same-sign operands the product is biased toward zero by an amount
+    that grows with the K accumulated in one place: at K = 4096 the whole-slice
+    accumulation measured a mean error of -2.2e-6 of |A||B|, the folded one
+    -5.1e-7.  Checked: the folded mean within 1e-6, and the elementwise bound."""
+    monkeypatch.setenv("AD_GEMM_FOLD", "4")
+    rng = np.random.default_rng(5)
+    A = rng.uniform(0, 1, (512, 4096)).astype(np.float32)
+    B = rng.uniform(0, 1, (4096, 512)).astype(np.float32)
+    got, kinds = run(dot_proc(A, B), "tc")
+    assert "gemm_tcgen05" in kinds
+    want = A.astype(np.float64) @ B.astype(np.float64)
+    mag = np.abs(A).astype(np.float64) @ np.abs(B).astype(np.float64)
+    assert abs(float(np.mean((got - want) / mag))) < 1e-6
+    assert np.all(np.abs(got - want) <= 1e-4 * mag + 1e-5)
