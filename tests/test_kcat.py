@@ -67,3 +67,57 @@ def test_encoder_products_folded(case, world, n):
     folded = [c for c in _loop_body(q) if type(c).__name__ == "DPElwFuse"
               and c.init_node.children_shapes[0][1] == 3 * heads * 64]
     assert len(folded) == n // (3 * heads - 1)
+
+
+def _synthetic(reader_between: bool):
+    """C = A0 @ W0 + A1 @ W1 as the reference's fusion emits it: the product
+    A1 @ W1 as its own command, W1 updated in place (``W1 += 1``) after it, and
+    a ``DPElwFuse`` whose dot A0 @ W0 heads an ADD of the product.  With
+    ``reader_between`` a command between the update and the sum reads W1, so
+    the update cannot move past it."""
+    rng = np.random.default_rng(1)
+    M, K, N = 64, 32, 48
+    G = ir.Gid()
+
+    def rm(ld):
+        return ir.Bin("Add", ir.Bin("Mult", ir.Xv(), ir.Const(ld)), ir.Yv())
+
+    arrs = {1: (M, K), 2: (K, N), 3: (M, K), 4: (K, N)}
+    cmds = [ir.AllocEntry(i, a * b, rng.standard_normal(a * b).astype(np.float32)) for i, (a, b) in arrs.items()]
+    cmds += [ir.AllocEntry(5, M * N), ir.AllocEntry(6, M * N), ir.AllocEntry(7, K * N)]
+    cmds.append(ir.DotProdNode(5, [ir.KMatrix(3, rm(K), [M, K]), ir.KMatrix(4, rm(N), [K, N])],
+                               ir.KMatrix(5, rm(N), [M, N]), [M, N], [[M, K], [K, N]]))
+    cmds.append(ir.BinaryNode(4, "ADD", [ir.KMatrix(4, G, [K, N]), ir.KConstant(1.0)],
+                              ir.KMatrix(4, G, [K, N]), [K, N], True))
+    if reader_between:
+        cmds.append(ir.BinaryNode(7, "MULT", [ir.KMatrix(4, G, [K, N]), ir.KConstant(2.0)],
+                                  ir.KMatrix(7, G, [K, N]), [K, N]))
+    nodes = [ir.AllocEntry(8, M * N, None, True),
+             ir.DotProdNode(8, [ir.KMatrix(1, rm(K), [M, K]), ir.KMatrix(2, rm(N), [K, N])],
+                            ir.KMatrix(8, None, [M, N], True), [M, N], [[M, K], [K, N]]),
+             ir.BinaryNode(6, "ADD", [ir.KMatrix(8, None, [M, N], True), ir.KMatrix(5, G, [M, N])],
+                           ir.KMatrix(6, G, [M, N]), [M, N])]
+    cmds.append(ir.DPElwFuse(nodes, 1))
+    outs = [ir.KMatrix(6, G, [M, N]), ir.KMatrix(4, G, [K, N])]
+    if reader_between:
+        outs.append(ir.KMatrix(7, G, [K, N]))
+    cmds.append(ir.Receiver(99, outs, "out"))
+    return ir.Proc(cmds)
+
+
+@pytest.mark.parametrize("reader_between", [False, True])
+def test_update_between_product_and_sum(monkeypatch, reader_between):
+    monkeypatch.setattr(kcat, "MIN_TERMS", 1)
+    want = _run(_synthetic(reader_between))
+    q = _synthetic(reader_between)
+    n = kcat.fuse_ksums(q)
+    kinds = [type(c).__name__ for c in q.procedure]
+    if reader_between:
+        # the update must stay before its reader, so the product stays before the update
+        assert n == 0 and kinds.count("DotProdNode") == 1
+    else:
+        # folded; the update now runs after the sum, which reads the weight before it
+        assert n == 1 and "DotProdNode" not in kinds
+        assert kinds.index("BinaryNode") > kinds.index("DPElwFuse")
+    for g, w in zip(_run(q), want):
+        np.testing.assert_allclose(g, w, rtol=1e-5, atol=1e-5)
